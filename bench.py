@@ -1,0 +1,326 @@
+"""Benchmark: block-sparse attention TFLOP/s (executed FLOPs) on 1..8 B200.
+
+Default workload (the one the metric is quoted on at
+1/2/4/8 GPUs): a head-sharded full-stack step — 30 attention layers of the
+Matrix-Game shape (24 heads, head_dim 128, 30x52 latent, 4-frame query chunk,
+64-frame memory, 3D blocks (4,4,8), keep 25%, cosine selection), QKV/O
+projections of hidden 3072 (random-init bf16), Ulysses all-to-all over NCCL
+before and after each attention when N > 1. ``--workload mg_layer`` runs
+BASELINE config 3 instead (single MG-shaped layer with the pruned-memory gather).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload W]
+
+One JSON line on rank 0. ``value`` = executed sparse-attention FLOPs of every
+layer on every rank / device time of the K timed steps (max over ranks).
+``e2e`` = the same metric with each step's input hidden states copied from
+pinned host memory and its output copied back inside the timed region.
+``--impl reference`` times the reference's CPU path (the oracle port: its
+block-mask logic + dense masked torch attention) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "sparse-attn fwd ms/call & TFLOP/s (executed FLOPs) at 1/2/4/8 B200 vs roofline"
+UNIT = "TFLOP/s"
+
+
+def _peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops"), d.get("bf16_tflops_sustained"), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def _profile_traffic(kernel_tag):
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary
+    (a line ``traffic_bytes_per_launch: <int>`` in profiles/<kernel_tag>*.md)."""
+    import glob
+    for path in sorted(glob.glob(os.path.join(REPO, "profiles", kernel_tag + "*.md"))):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
+        if m:
+            return int(m.group(1)), os.path.basename(path)
+    return None, None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        loaded = [x for x in sm if x > 0.5 * (mx or max(sm))] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference path (oracle port) — cpu_baseline and --impl reference
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(cfg, heads=1, seed=3):
+    """One bounded sample of the workload on the host: pooled-score selection
+    (reference rules) + dense masked torch attention for ``heads`` heads of one
+    layer. Returns (seconds, executed sparse FLOPs of the sample, threads)."""
+    from oracle import li_oracle as O
+    threads = torch.get_num_threads()
+    LH, LW = cfg.latent_hw
+    tile = cfg.tile
+    bs = tile[0] * tile[1] * tile[2]
+    g = torch.Generator().manual_seed(seed)
+    D = cfg.head_dim
+    q = torch.randn(1, heads, cfg.q_tokens, D, generator=g).to(torch.bfloat16).float().numpy()
+    k = torch.randn(1, heads, cfg.kv_frames * cfg.frame_tokens, D, generator=g).to(torch.bfloat16).float().numpy()
+    v = torch.randn(1, heads, cfg.kv_frames * cfg.frame_tokens, D, generator=g).to(torch.bfloat16).float().numpy()
+    t0 = time.perf_counter()
+    qt, qp = O.tile_pool(q, cfg.query_frames, LH, LW, tile, "bf16")
+    kt, kp = O.tile_pool(k, cfg.kv_frames, LH, LW, tile, "bf16")
+    vt = O.tile_raster(v, cfg.kv_frames, LH, LW, tile)
+    gk = O.grid_dims(cfg.kv_frames, LH, LW, tile)
+    nq, nk = cfg.blocks()
+    idx, cnt = O.generate_prefill_indices(qp, kp, 0, gk, dict(tile_size=tile, topk_ratio=cfg.keep_ratio,
+                                                              sim_metric=cfg.metric), "bf16", q_offset=nk - nq)
+    qtt, ktt, vtt = (torch.from_numpy(np.ascontiguousarray(a)) for a in (qt, kt, vt))
+    kflat = ktt.reshape(1, heads, nk * bs, D)
+    vflat = vtt.reshape(1, heads, nk * bs, D)
+    for h in range(heads):
+        for i in range(nq):
+            mask = torch.zeros(nk, dtype=torch.bool)
+            mask[torch.from_numpy(idx[0, h, i, :cnt[0, h, i]].astype(np.int64))] = True
+            m = mask.repeat_interleave(bs)[None, :].expand(bs, -1)
+            torch.nn.functional.scaled_dot_product_attention(qtt[0, h, i][None], kflat[0, h][None],
+                                                             vflat[0, h][None], attn_mask=m[None])
+    dt = time.perf_counter() - t0
+    return dt, cfg.attention_flops(heads), threads
+
+
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(max(0, args.warmup_ref)):
+        cpu_reference_sample(cfg)
+    times, flops = [], 0.0
+    for s in range(args.steps):
+        dt, fl, threads = cpu_reference_sample(cfg, seed=10 + s)
+        times.append(dt)
+        flops += fl
+    value = flops / sum(times) / 1e12
+    sample = (f"1 head of 1 layer per step ({cfg.query_frames}-frame query chunk vs {cfg.kv_frames}-frame K/V, "
+              f"{cfg.blocks()[0]} query blocks x {cfg.budget()} selected blocks): block-mask logic + dense masked "
+              f"SDPA in fp32 on bf16-valued inputs")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(cfg, args, world),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(cfg, args, world):
+    nq, nk = cfg.blocks()
+    return {"workload": "config5_head_sharded_stack" if args.workload == "stack" else "config3_mg_layer",
+            "layers": cfg.layers, "heads": cfg.heads, "head_dim": cfg.head_dim, "hidden": cfg.hidden,
+            "latent_hw": list(cfg.latent_hw), "query_frames": cfg.query_frames,
+            "memory_frames": cfg.memory_frames, "tile": list(cfg.tile), "keep_ratio": cfg.keep_ratio,
+            "sim_metric": cfg.metric, "q_blocks": nq, "k_blocks": nk, "selected_blocks": cfg.budget(),
+            "attn_tflop_per_call": cfg.attention_flops() / 1e12,
+            "parallelism": f"ulysses_heads{world}", "l2": "inputs larger than L2 (resident K/V >> 126 MB)"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_gpu(args, cfg, rank, world, local_rank):
+    from light_interaction_project_b200 import _lib as L
+    from light_interaction_project_b200 import kernels as K
+    from light_interaction_project_b200.ulysses import HeadShardedStack
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L.load()
+    launches = {"n": 0}
+    for name in ("pool_blocks", "select_blocks", "sparse_attn_raster", "gather_frames"):
+        orig = getattr(K, name)
+
+        def wrap(*a, __orig=orig, **kw):
+            launches["n"] += 1  # each wrapper issues exactly one kernel launch
+            return __orig(*a, **kw)
+        setattr(K, name, wrap)
+    group = dist.group.WORLD if world > 1 else None
+    stack = HeadShardedStack(cfg, rank, world, dev, group=group)
+    x0 = stack.make_input()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # Warm-up.
+    for _ in range(args.warmup):
+        stack.step(x0)
+    barrier()
+    K.raise_device_errors(dev)
+
+    # Device-resident timing, with per-layer attention events on one step.
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(cfg.layers)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches["n"] = 0
+    barrier()
+    with ClockSampler(local_rank) as clk:
+        start.record()
+        for s in range(args.steps):
+            stack.step(x0, ev if s == args.steps - 1 else None)
+        end.record()
+        barrier()
+    n_launch = launches["n"]
+    ms = start.elapsed_time(end)
+    attn_ms = [a.elapsed_time(b) for a, b in ev]
+    # End-to-end: host input -> device, step, device output -> host.
+    x_host = x0.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        xd = x_host.to(dev, non_blocking=True)
+        y = stack.step(xd)
+        y_host.copy_(y, non_blocking=True)
+    e2.record()
+    barrier()
+    ms_e2e = s2.elapsed_time(e2)
+    K.raise_device_errors(dev)
+
+    t = torch.tensor([ms, ms_e2e, sum(attn_ms) / len(attn_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e, attn_call_ms = t.tolist()
+    if rank != 0:
+        return
+    total_flops = cfg.attention_flops() * cfg.layers * args.steps
+    value = total_flops / (ms * 1e-3) / 1e12
+    e2e_value = total_flops / (ms_e2e * 1e-3) / 1e12
+    burst, sustained, kind = _peaks()
+    per_launch_flops = cfg.attention_flops(cfg.heads // world)
+    achieved = per_launch_flops / (attn_call_ms * 1e-3) / 1e12
+    traffic, tfile = _profile_traffic("attn_fwd_config5")
+    if traffic is not None and world != 1:
+        traffic = traffic // world
+    cpu_s, cpu_fl, threads = cpu_reference_sample(cfg)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "ms_per_call": attn_call_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden states, random-init bf16 weights, random resident K/V memory)",
+        "config": workload_config(cfg, args, world),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": achieved / sustained, "traffic": traffic,
+                     "peak_kind": f"{kind} bf16 sustained (burst {burst})",
+                     "traffic_source": tfile},
+        "cpu_baseline": {"value": cpu_fl / cpu_s / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "1 head of 1 layer: block-mask logic + dense masked SDPA (fp32) on the host"},
+        "e2e": {"value": e2e_value, "unit": UNIT,
+                "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size() * world),
+                "d2h_bytes_per_step": int(y_host.numel() * y_host.element_size() * world)},
+        "gpu_launches": int(n_launch * world),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="stack", choices=["stack"])
+    ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--warmup-ref", type=int, default=0)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    from light_interaction_project_b200.ulysses import StackConfig
+    cfg = StackConfig(layers=args.layers)
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, world)
+        return
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_gpu(args, cfg, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

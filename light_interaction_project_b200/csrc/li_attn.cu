@@ -1,0 +1,762 @@
+// Block-sparse attention forward for sm_100a: TMA + tcgen05 + TMEM.
+//
+// One CTA computes one query block (bs rows, padded to the 128-row MMA tile)
+// of one (b, h) against the key blocks in its index list. Six warps:
+//   warps 0-3  softmax / correction / epilogue — thread t owns query row t,
+//              which is TMEM lane t (warp w reads its lane quarter 32w..32w+31);
+//   warp 4     TMA producer — Q once, then K_j and V_j of every selected block;
+//   warp 5     MMA issuer (one elected lane) + TMEM allocator.
+// TMEM columns: S = Q K^T (fp32, bs columns) at 0, O (fp32, D columns) at 128.
+// The softmax writes P as packed 16-bit pairs over the first bs/2 columns of S,
+// and the PV product reads it from there as the TMEM A operand (TS form), so P
+// never touches shared memory.
+//
+// Per key block j:  MMA  S = Q K_j^T                -> commit k_empty, s_full
+//                   SM   row max, lazy O rescale, P = exp2(S*c - m) -> p_full
+//                   MMA  O (+)= P V_j                -> commit v_empty, o_full
+// The row max is only moved (and O rescaled) when it grows by more than 8 in
+// log2 units; otherwise the stale max is kept (P <= 2^8), which leaves O/l
+// exact. The producer refills K_{j+1} as soon as S_j completes and V_{j+1} as
+// soon as PV_j completes. Two CTAs share an SM (96 KB smem, 256 TMEM columns
+// each), so one CTA's softmax overlaps the other's MMAs.
+//
+// Operands come straight from the caller's layout through 5-D tensor maps
+// (d, w, h, t, b*h): a 3D (tt, th, tw) block of a raster tensor is one box, and
+// TMA fills coordinates past the grid edge with zeros — exactly the zero
+// padding of the tiled layout. The epilogue stores O through the same kind of
+// map, and TMA drops the rows that fall outside the tensor (untiling for free).
+//
+// Every mbarrier wait is bounded (kTimeoutNs); on expiry the CTA records
+// LI_DEVERR_TIMEOUT, drains its own copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <algorithm>
+
+#include "li_common.cuh"
+
+namespace li {
+namespace attn {
+
+constexpr int kMaxMaps = 4;
+constexpr int kThreads = 192;
+constexpr uint64_t kTimeoutNs = 1000000000ull;  // 1 s per wait
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0, kColO = 128;
+
+struct __align__(64) Params {
+  CUtensorMap q_map[kMaxMaps];
+  CUtensorMap k_map[kMaxMaps];
+  CUtensorMap v_map[kMaxMaps];
+  CUtensorMap kt_map[kMaxMaps];
+  CUtensorMap vt_map[kMaxMaps];
+  CUtensorMap o_map[kMaxMaps];
+  const int32_t* idx;
+  int64_t i_b, i_h, i_q, i_s;
+  const int32_t* cnt;
+  int64_t c_b, c_h, c_q;
+  float* lse;
+  int64_t lse_len;
+  uint32_t* err;
+  float scale_log2;
+  int32_t H, b0, per_batch;
+  int32_t q_raster, kv_raster;
+  int32_t q_nh, q_nw, q_tt, q_th, q_tw;
+  int32_t k_nh, k_nw, k_tt, k_th, k_tw;
+  int32_t ntxt, n_kv, nq;
+  int32_t smax;  // index-row width: counts are clamped to it
+};
+
+// ------------------------------- PTX helpers -------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait. Returns false when the CTA is aborting (another warp timed
+// out) or this wait ran past kTimeoutNs (then it raises the abort itself).
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                       uint32_t* err, bool honour_abort = true) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 7) == 0) {
+      if (honour_abort && *abort_flag) return false;
+      if (gtimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        if (err) atomicOr(err, (unsigned)LI_DEVERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, const int c[5], uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(c[4]), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, uint32_t src, const int c[5]) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(c[4]), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_commit_and_drain() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t r;
+  if (F16) asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout: start>>4
+// [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version 1 at bit 46, swizzle 2 at [61,64)).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16 with fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool f16, bool b_mn_major) {
+  return (1u << 4) | ((f16 ? 0u : 1u) << 7) | ((f16 ? 0u : 1u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// --------------------------------- kernel ----------------------------------
+template <int D, int BS>
+struct Smem {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kQHalf = 128 * 128;  // 128 rows of 128 bytes
+  static constexpr int kKVHalf = BS * 128;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kHalves * kQHalf;
+  static constexpr int kOffV = kOffK + kHalves * kKVHalf;
+  static constexpr int kOffBar = kOffV + kHalves * kKVHalf;
+  static constexpr int kBytes = kOffBar + 128 + 1024;  // + alignment slack
+  static constexpr uint32_t kTileBytes = (uint32_t)kHalves * BS * 128;
+};
+
+__device__ __forceinline__ void block_coords(int raster, int blk, int bsz, int nh, int nw, int tt, int th, int tw,
+                                             int w, int c[5]) {
+  if (raster) {
+    const int cw = blk % nw, rem = blk / nw, ch = rem % nh, ct = rem / nh;
+    c[1] = cw * tw; c[2] = ch * th; c[3] = ct * tt;
+  } else {
+    c[1] = blk * bsz; c[2] = 0; c[3] = 0;
+  }
+  c[0] = 0;
+  c[4] = w;
+}
+
+template <int D, int BS, bool F16>
+__global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_constant__ Params p) {
+  using L = Smem<D, BS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qi = blockIdx.x;
+  const int bl = blockIdx.y / p.H, h = blockIdx.y % p.H;
+  const int b = p.b0 + bl;
+  const int mi = p.per_batch ? bl : 0;
+  const int wc = p.per_batch ? h : b * p.H + h;
+
+  const uint32_t bar_q = sb + L::kOffBar, bar_kf = bar_q + 8, bar_ke = bar_q + 16, bar_vf = bar_q + 24,
+                 bar_ve = bar_q + 32, bar_s = bar_q + 40, bar_p = bar_q + 48, bar_o = bar_q + 56,
+                 bar_fin = bar_q + 64;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffBar + 72);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffBar + 76);
+
+  const int S_raw = p.cnt[b * p.c_b + h * p.c_h + (int64_t)qi * p.c_q];
+  const int S = S_raw < 0 ? 0 : (S_raw > p.smax ? p.smax : S_raw);
+  if (S != S_raw && threadIdx.x == 0 && p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
+  const int32_t* irow = p.idx + b * p.i_b + h * p.i_h + (int64_t)qi * p.i_q;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1); mbar_init(bar_kf, 1); mbar_init(bar_ke, 1); mbar_init(bar_vf, 1);
+    mbar_init(bar_ve, 1); mbar_init(bar_s, 1); mbar_init(bar_p, 4); mbar_init(bar_o, 1); mbar_init(bar_fin, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(smem_u32(smem + L::kOffBar + 72), kTmemCols);
+  if (BS < 128 && warp < 4) {
+    // Query rows past the block are zero so the padded MMA rows stay finite.
+    for (int hf = 0; hf < L::kHalves; ++hf) {
+      uint4* z = reinterpret_cast<uint4*>(smem + L::kOffQ + hf * L::kQHalf + BS * 128);
+      for (int i = threadIdx.x; i < (128 - BS) * 8; i += 128) z[i] = make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0 && S > 0) {
+      int c[5];
+      block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+      mbar_expect_tx(bar_q, L::kTileBytes);
+      for (int hf = 0; hf < L::kHalves; ++hf) {
+        c[0] = 64 * hf;
+        tma_load_5d(sb + L::kOffQ + hf * L::kQHalf, &p.q_map[mi], c, bar_q);
+      }
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < S; ++j) {
+        int blk = irow[(int64_t)j * p.i_s];
+        if (blk < 0 || blk >= p.n_kv) {
+          if (p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
+          blk = 0;
+        }
+        const CUtensorMap* km;
+        const CUtensorMap* vm;
+        if (p.kv_raster && blk < p.ntxt) {
+          block_coords(0, blk, BS, 1, 1, 1, 1, 1, wc, c);
+          km = &p.kt_map[mi]; vm = &p.vt_map[mi];
+        } else {
+          block_coords(p.kv_raster, p.kv_raster ? blk - p.ntxt : blk, BS, p.k_nh, p.k_nw, p.k_tt, p.k_th, p.k_tw,
+                       wc, c);
+          km = &p.k_map[mi]; vm = &p.v_map[mi];
+        }
+        if (j > 0 && !mbar_wait(bar_ke, (j - 1) & 1, abort_flag, p.err)) break;
+        mbar_expect_tx(bar_kf, L::kTileBytes);
+        for (int hf = 0; hf < L::kHalves; ++hf) {
+          c[0] = 64 * hf;
+          tma_load_5d(sb + L::kOffK + hf * L::kKVHalf, km, c, bar_kf);
+        }
+        issued_k = j + 1;
+        if (j > 0 && !mbar_wait(bar_ve, (j - 1) & 1, abort_flag, p.err)) break;
+        mbar_expect_tx(bar_vf, L::kTileBytes);
+        for (int hf = 0; hf < L::kHalves; ++hf) {
+          c[0] = 64 * hf;
+          tma_load_5d(sb + L::kOffV + hf * L::kKVHalf, vm, c, bar_vf);
+        }
+        issued_v = j + 1;
+      }
+      if (*abort_flag) {
+        // Drain this CTA's own loads before shared memory is released.
+        mbar_wait(bar_q, 0, abort_flag, nullptr, false);
+        if (issued_k) mbar_wait(bar_kf, (issued_k - 1) & 1, abort_flag, nullptr, false);
+        if (issued_v) mbar_wait(bar_vf, (issued_v - 1) & 1, abort_flag, nullptr, false);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0 && S > 0) {
+      constexpr uint32_t idS = idesc_f16(128, BS, F16, false);
+      constexpr uint32_t idPV = idesc_f16(128, D, F16, true);
+      bool issued = false;
+      if (mbar_wait(bar_q, 0, abort_flag, p.err)) {
+        tc_fence_after();
+        for (int j = 0; j < S; ++j) {
+          if (!mbar_wait(bar_kf, j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = sdesc(sb + L::kOffQ + (kk >> 2) * L::kQHalf + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc(sb + L::kOffK + (kk >> 2) * L::kKVHalf + (kk & 3) * 32, 16, 1024);
+            mma_ss(tmem + kColS, ad, bd, idS, kk > 0 ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit(bar_ke);
+          mma_commit(bar_s);
+          if (!mbar_wait(bar_p, j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
+          if (!mbar_wait(bar_vf, j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BS / 16; ++kk) {
+            const uint64_t bd = sdesc(sb + L::kOffV + kk * 2048, L::kKVHalf, 1024);
+            mma_ts(tmem + kColO, tmem + kColS + kk * 8, bd, idPV, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar_ve);
+          mma_commit(bar_o);
+        }
+      }
+      if (issued) {
+        // All MMAs of this CTA complete before TMEM is released.
+        mma_commit(bar_fin);
+        mbar_wait(bar_fin, 0, abort_flag, p.err, false);
+      }
+    }
+  } else {
+    // ------------------------ softmax + epilogue ---------------------------
+    const int row = threadIdx.x;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_base + kColS, tO = tmem + lane_base + kColO;
+    const float c2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < S && ok; ++j) {
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s, j & 1, abort_flag, p.err));
+      if (!ok) break;
+      tc_fence_after();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < BS / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tS + cc * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+      }
+      const float m_new = fmaxf(m, mx * c2);
+      const bool need = (j > 0) && (m_new - m > 8.0f);
+      float alpha = 1.f;
+      if (j == 0) {
+        m = m_new;
+      } else if (need) {
+        alpha = ex2(m - m_new);
+        m = m_new;
+      }
+      if (__any_sync(0xFFFFFFFFu, need)) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o, (j - 1) & 1, abort_flag, p.err));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tO + cc * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tmem_st32(tO + cc * 32, r);
+        }
+        tmem_wait_st();
+      }
+      l *= alpha;
+#pragma unroll
+      for (int cc = 0; cc < BS / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tS + cc * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2(fmaf(__uint_as_float(r[2 * e]), c2, -m));
+          const float p1 = ex2(fmaf(__uint_as_float(r[2 * e + 1]), c2, -m));
+          l += p0 + p1;
+          pk[e] = pack2<F16>(p0, p1);
+        }
+        tmem_st16(tS + cc * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p);
+    }
+    if (ok && S > 0) {
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o, (S - 1) & 1, abort_flag, p.err));
+      tc_fence_after();
+    }
+    // Named barrier 1: every softmax warp knows whether the CTA aborted.
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const bool store = ok && !*abort_flag;
+    if (store) {
+      const float inv = S > 0 ? 1.f / l : 0.f;
+      uint8_t* stage = smem + L::kOffQ;
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t r[32];
+        if (S > 0) {
+          tmem_ld32(tO + cc * 32, r);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = 0u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack2<F16>(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+        const int col0 = cc * 32, hf = col0 / 64, ch0 = (col0 % 64) / 8;
+        uint8_t* rowp = stage + hf * L::kQHalf + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int phys = (ch0 + q) ^ (row & 7);
+          *reinterpret_cast<uint4*>(rowp + phys * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (store && threadIdx.x == 0) {
+      int c[5];
+      block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+      for (int hf = 0; hf < L::kHalves; ++hf) {
+        c[0] = 64 * hf;
+        tma_store_5d(&p.o_map[mi], sb + L::kOffQ + hf * L::kQHalf, c);
+      }
+      tma_store_commit_and_drain();
+    }
+    if (store && p.lse && row < BS)
+      p.lse[(int64_t)(b * p.H + h) * p.lse_len + (int64_t)qi * BS + row] = S > 0 ? m + __log2f(l) : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------ host side ----------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Describes one operand as a 5-D tensor (d, x, y, z, w) for TMA.
+struct MapSpec {
+  const void* base;
+  uint64_t dims[5];
+  uint64_t strides[4];  // bytes, dims 1..4
+  uint32_t box[5];
+};
+
+li_status encode(CUtensorMap* out, const MapSpec& s, bool f16, const char* name) {
+  auto fn = get_encode();
+  if (!fn) return fail(LI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5], es[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < 5; ++i) { dims[i] = s.dims[i]; box[i] = s.box[i]; }
+  for (int i = 0; i < 4; ++i) {
+    strides[i] = s.strides[i];
+    if (strides[i] % 16 || strides[i] >= (1ull << 40))
+      return fail(LI_ERR_ALIGNMENT, "%s: stride %d (%llu bytes) is not a multiple of 16 below 2^40", name, i + 1,
+                  (unsigned long long)strides[i]);
+  }
+  for (int i = 0; i < 5; ++i)
+    if (dims[i] == 0 || dims[i] > (1ull << 32)) return fail(LI_ERR_SHAPE, "%s: dim %d out of range", name, i);
+  if (!aligned16(s.base)) return fail(LI_ERR_ALIGNMENT, "%s: base pointer not 16-byte aligned", name);
+  CUresult r = fn(out, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5,
+                  const_cast<void*>(s.base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LI_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return LI_OK;
+}
+
+// How the (b, h) pair is addressed: merged into one dim, or one map per batch.
+struct BHPlan {
+  bool merged;
+  uint64_t w_dim;
+  int64_t w_stride;  // elements
+};
+
+BHPlan plan_bh(const li_view4& v) {
+  const int64_t B = v.shape[0], H = v.shape[1];
+  BHPlan pl;
+  if (B == 1) { pl.merged = true; pl.w_dim = (uint64_t)H; pl.w_stride = v.stride[1]; }
+  else if (H == 1) { pl.merged = true; pl.w_dim = (uint64_t)B; pl.w_stride = v.stride[0]; }
+  else if (v.stride[0] == H * v.stride[1]) { pl.merged = true; pl.w_dim = (uint64_t)(B * H); pl.w_stride = v.stride[1]; }
+  else { pl.merged = false; pl.w_dim = (uint64_t)H; pl.w_stride = v.stride[1]; }
+  return pl;
+}
+
+// Raster operand: (d, w, h, t, bh); box = one (tt, th, tw) block.
+MapSpec raster_spec(const li_view4& v, const li_grid3d& g, const BHPlan& pl, int b, int es) {
+  MapSpec s;
+  const int64_t sl = v.stride[2] * es;
+  s.base = static_cast<const uint8_t*>(v.data) + (pl.merged ? 0 : b * v.stride[0] * es);
+  s.dims[0] = (uint64_t)v.shape[3]; s.dims[1] = (uint64_t)g.LW; s.dims[2] = (uint64_t)g.LH;
+  s.dims[3] = (uint64_t)(v.shape[2] / ((int64_t)g.LH * g.LW)); s.dims[4] = pl.w_dim;
+  s.strides[0] = (uint64_t)sl; s.strides[1] = (uint64_t)(sl * g.LW); s.strides[2] = (uint64_t)(sl * g.LW * g.LH);
+  s.strides[3] = (uint64_t)(pl.w_stride * es);
+  s.box[0] = 64; s.box[1] = (uint32_t)g.tw; s.box[2] = (uint32_t)g.th; s.box[3] = (uint32_t)g.tt; s.box[4] = 1;
+  return s;
+}
+
+// Row operand: (d, rows, 1, 1, bh); box = bs consecutive rows.
+MapSpec rows_spec(const li_view4& v, int bs, const BHPlan& pl, int b, int es) {
+  MapSpec s;
+  const int64_t sl = v.stride[2] * es;
+  s.base = static_cast<const uint8_t*>(v.data) + (pl.merged ? 0 : b * v.stride[0] * es);
+  s.dims[0] = (uint64_t)v.shape[3]; s.dims[1] = (uint64_t)v.shape[2]; s.dims[2] = 1; s.dims[3] = 1;
+  s.dims[4] = pl.w_dim;
+  s.strides[0] = (uint64_t)sl;
+  s.strides[1] = (uint64_t)(sl * v.shape[2] + 15) / 16 * 16;
+  s.strides[2] = s.strides[1];
+  s.strides[3] = (uint64_t)(pl.w_stride * es);
+  s.box[0] = 64; s.box[1] = (uint32_t)bs; s.box[2] = 1; s.box[3] = 1; s.box[4] = 1;
+  return s;
+}
+
+using KernelFn = void (*)(Params);
+
+template <int D, int BS, bool F16>
+li_status launch_t(const Params& prm, dim3 grid, cudaStream_t stream) {
+  using L = Smem<D, BS>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D, BS, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kBytes);
+    if (e != cudaSuccess) return cuda_status(e, "attention smem attribute");
+    configured = true;
+  }
+  attn_fwd_kernel<D, BS, F16><<<grid, kThreads, L::kBytes, stream>>>(prm);
+  return cuda_status(cudaGetLastError(), "attention kernel launch");
+}
+
+li_status launch(int D, int BS, bool f16, const Params& prm, dim3 grid, cudaStream_t s) {
+  if (D == 128 && BS == 128) return f16 ? launch_t<128, 128, true>(prm, grid, s) : launch_t<128, 128, false>(prm, grid, s);
+  if (D == 128 && BS == 64) return f16 ? launch_t<128, 64, true>(prm, grid, s) : launch_t<128, 64, false>(prm, grid, s);
+  if (D == 64 && BS == 128) return f16 ? launch_t<64, 128, true>(prm, grid, s) : launch_t<64, 128, false>(prm, grid, s);
+  if (D == 64 && BS == 64) return f16 ? launch_t<64, 64, true>(prm, grid, s) : launch_t<64, 64, false>(prm, grid, s);
+  return fail(LI_ERR_UNSUPPORTED, "attention built for D in {64,128} and block size in {64,128} (got D=%d bs=%d)", D, BS);
+}
+
+li_status check_operand(const li_view4* v, const char* name, int dtype, int64_t B, int64_t H, int64_t D) {
+  if (!v || !v->data) return fail(LI_ERR_INVALID_ARG, "%s is required", name);
+  if (v->dtype != dtype) return fail(LI_ERR_INVALID_ARG, "%s: dtype differs from q", name);
+  if (v->shape[0] != B || v->shape[1] != H || v->shape[3] != D)
+    return fail(LI_ERR_SHAPE, "%s: expected [B=%lld, H=%lld, *, D=%lld]", name, (long long)B, (long long)H, (long long)D);
+  if (v->stride[3] != 1) return fail(LI_ERR_STRIDE, "%s: head dim must be contiguous", name);
+  if (!aligned16(v->data)) return fail(LI_ERR_ALIGNMENT, "%s: base pointer not 16-byte aligned", name);
+  return LI_OK;
+}
+
+// Shared driver of both public forms.
+li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_view4* k, const li_view4* v,
+              bool kv_raster, const li_grid3d* gk, const li_view4* kt, const li_view4* vt, int bs,
+              const li_index_view* idx, float sm_scale, li_view4* o, float* lse, uint32_t* err, void* stream) {
+  if (!q || !q->data) return fail(LI_ERR_INVALID_ARG, "q is required");
+  const int dtype = q->dtype;
+  if (dtype != LI_DTYPE_BF16 && dtype != LI_DTYPE_FP16)
+    return fail(LI_ERR_UNSUPPORTED, "attention runs on bf16 or fp16 operands (got dtype %d)", dtype);
+  const bool f16 = dtype == LI_DTYPE_FP16;
+  const int es = 2;
+  const int64_t B = q->shape[0], H = q->shape[1], D = q->shape[3];
+  if (D != 64 && D != 128) return fail(LI_ERR_UNSUPPORTED, "head dim %lld (built for 64 and 128)", (long long)D);
+  if (bs != 64 && bs != 128) return fail(LI_ERR_UNSUPPORTED, "block size %d (built for 64 and 128)", bs);
+  for (const li_view4* t : {q, k, v, (const li_view4*)o})
+    if (li_status st = check_operand(t, t == q ? "q" : t == k ? "k" : t == v ? "v" : "o", dtype, B, H, D)) return st;
+  if (o->shape[2] != q->shape[2]) return fail(LI_ERR_SHAPE, "o must have q's shape");
+  for (int i = 0; i < 4; ++i)
+    if (k->shape[i] != v->shape[i]) return fail(LI_ERR_SHAPE, "k and v shapes differ");
+  if (!idx || !idx->indices || !idx->counts) return fail(LI_ERR_INVALID_ARG, "index view required");
+  if (idx->shape[0] != B || idx->shape[1] != H) return fail(LI_ERR_SHAPE, "indices: leading dims must be [B, H]");
+
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  int64_t nq, n_kv;
+  int ntxt = 0;
+  if (q_raster) {
+    const int64_t HW = (int64_t)gq->LH * gq->LW;
+    if ((int64_t)gq->tt * gq->th * gq->tw != bs) return fail(LI_ERR_SHAPE, "grid_q tile does not give bs");
+    if (q->shape[2] != (int64_t)gq->T * HW) return fail(LI_ERR_SHAPE, "q length must be T*LH*LW of grid_q");
+    if (gq->tw > 256 || gq->th > 256 || gq->tt > 256) return fail(LI_ERR_UNSUPPORTED, "tile dims must be <= 256");
+    prm.q_nh = (int)ceil_div(gq->LH, gq->th); prm.q_nw = (int)ceil_div(gq->LW, gq->tw);
+    prm.q_tt = gq->tt; prm.q_th = gq->th; prm.q_tw = gq->tw;
+    nq = ceil_div(gq->T, gq->tt) * prm.q_nh * prm.q_nw;
+  } else {
+    nq = ceil_div(q->shape[2], bs);
+  }
+  if (kv_raster) {
+    const int64_t HW = (int64_t)gk->LH * gk->LW;
+    if ((int64_t)gk->tt * gk->th * gk->tw != bs) return fail(LI_ERR_SHAPE, "grid_k tile does not give bs");
+    if (k->shape[2] != (int64_t)gk->T * HW) return fail(LI_ERR_SHAPE, "k_vis length must be T*LH*LW of grid_k");
+    prm.k_nh = (int)ceil_div(gk->LH, gk->th); prm.k_nw = (int)ceil_div(gk->LW, gk->tw);
+    prm.k_tt = gk->tt; prm.k_th = gk->th; prm.k_tw = gk->tw;
+    if ((kt == nullptr) != (vt == nullptr)) return fail(LI_ERR_INVALID_ARG, "k_txt and v_txt go together");
+    if (kt && kt->shape[2] > 0) {
+      if (li_status st = check_operand(kt, "k_txt", dtype, B, H, D)) return st;
+      if (li_status st = check_operand(vt, "v_txt", dtype, B, H, D)) return st;
+      if (kt->shape[2] != vt->shape[2]) return fail(LI_ERR_SHAPE, "k_txt and v_txt lengths differ");
+      ntxt = (int)ceil_div(kt->shape[2], bs);
+    }
+    n_kv = ntxt + ceil_div(gk->T, gk->tt) * prm.k_nh * prm.k_nw;
+  } else {
+    if (k->shape[2] % bs) return fail(LI_ERR_SHAPE, "K length (%lld) must be divisible by logical_block_size (%d)",
+                                      (long long)k->shape[2], bs);
+    n_kv = k->shape[2] / bs;
+  }
+  if (idx->shape[2] < nq) return fail(LI_ERR_SHAPE, "indices have %lld query blocks, need %lld",
+                                      (long long)idx->shape[2], (long long)nq);
+  if (n_kv > (1ll << 30) || nq > (1ll << 30)) return fail(LI_ERR_SHAPE, "too many blocks");
+  prm.idx = idx->indices; prm.i_b = idx->stride[0]; prm.i_h = idx->stride[1]; prm.i_q = idx->stride[2]; prm.i_s = idx->stride[3];
+  prm.cnt = idx->counts; prm.c_b = idx->count_stride[0]; prm.c_h = idx->count_stride[1]; prm.c_q = idx->count_stride[2];
+  prm.lse = lse; prm.lse_len = nq * bs; prm.err = err;
+  prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  prm.H = (int)H; prm.q_raster = q_raster; prm.kv_raster = kv_raster;
+  prm.ntxt = ntxt; prm.n_kv = (int)n_kv; prm.nq = (int)nq;
+  if (idx->shape[3] < 0 || idx->shape[3] > (1ll << 30)) return fail(LI_ERR_SHAPE, "bad index-row width");
+  prm.smax = (int)idx->shape[3];
+  if (nq == 0 || B * H == 0) return LI_OK;
+
+  // All operands share one (b, h) addressing plan; fall back to per-batch
+  // maps when any operand's batch and head strides do not merge.
+  const li_view4* ops[6] = {q, k, v, o, kt && ntxt ? kt : nullptr, vt && ntxt ? vt : nullptr};
+  bool merged = true;
+  for (const li_view4* t : ops)
+    if (t) merged = merged && plan_bh(*t).merged && (plan_bh(*t).w_dim == plan_bh(*q).w_dim || B == 1 || H == 1);
+  const int64_t chunk = merged ? B : kMaxMaps;
+  for (int64_t b0 = 0; b0 < B; b0 += chunk) {
+    const int64_t nb = std::min<int64_t>(chunk, B - b0);
+    prm.b0 = (int)b0;
+    prm.per_batch = merged ? 0 : 1;
+    for (int64_t i = 0; i < (merged ? 1 : nb); ++i) {
+      const int bb = (int)(b0 + i);
+      auto pl = [&](const li_view4& t) {
+        BHPlan x = plan_bh(t);
+        if (!merged) { x.merged = false; x.w_dim = (uint64_t)H; x.w_stride = t.stride[1]; }
+        return x;
+      };
+      li_status st;
+      if (q_raster) {
+        st = encode(&prm.q_map[i], raster_spec(*q, *gq, pl(*q), bb, es), f16, "q");
+        if (!st) st = encode(&prm.o_map[i], raster_spec(*o, *gq, pl(*o), bb, es), f16, "o");
+      } else {
+        st = encode(&prm.q_map[i], rows_spec(*q, bs, pl(*q), bb, es), f16, "q");
+        if (!st) st = encode(&prm.o_map[i], rows_spec(*o, bs, pl(*o), bb, es), f16, "o");
+      }
+      if (st) return st;
+      if (kv_raster) {
+        st = encode(&prm.k_map[i], raster_spec(*k, *gk, pl(*k), bb, es), f16, "k");
+        if (!st) st = encode(&prm.v_map[i], raster_spec(*v, *gk, pl(*v), bb, es), f16, "v");
+        if (!st && ntxt) st = encode(&prm.kt_map[i], rows_spec(*kt, bs, pl(*kt), bb, es), f16, "k_txt");
+        if (!st && ntxt) st = encode(&prm.vt_map[i], rows_spec(*vt, bs, pl(*vt), bb, es), f16, "v_txt");
+      } else {
+        st = encode(&prm.k_map[i], rows_spec(*k, bs, pl(*k), bb, es), f16, "k");
+        if (!st) st = encode(&prm.v_map[i], rows_spec(*v, bs, pl(*v), bb, es), f16, "v");
+      }
+      if (st) return st;
+    }
+    dim3 grid((unsigned)nq, (unsigned)(nb * H));
+    if (nb * H > 65535) return fail(LI_ERR_SHAPE, "B*H too large for one launch");
+    if (li_status st = launch((int)D, bs, f16, prm, grid, static_cast<cudaStream_t>(stream))) return st;
+  }
+  return LI_OK;
+}
+
+}  // namespace attn
+}  // namespace li
+
+using namespace li;
+
+extern "C" li_status li_sparse_attn_tiled(const li_view4* q, const li_view4* k, const li_view4* v,
+                                          const li_index_view* idx, int32_t bs, float sm_scale, li_view4* o,
+                                          float* lse, uint32_t* err_word, void* stream) {
+  return attn::run(q, false, nullptr, k, v, false, nullptr, nullptr, nullptr, bs, idx, sm_scale, o, lse, err_word,
+                   stream);
+}
+
+extern "C" li_status li_sparse_attn_raster(const li_view4* q, li_grid3d grid_q, const li_view4* k_txt,
+                                           const li_view4* v_txt, const li_view4* k_vis, const li_view4* v_vis,
+                                           li_grid3d grid_k, const li_index_view* idx, float sm_scale, li_view4* o,
+                                           float* lse, uint32_t* err_word, void* stream) {
+  if (grid_q.tt != grid_k.tt || grid_q.th != grid_k.th || grid_q.tw != grid_k.tw || grid_q.LH != grid_k.LH ||
+      grid_q.LW != grid_k.LW)
+    return fail(LI_ERR_SHAPE, "grid_q and grid_k must share the latent size and tile");
+  const int bs = grid_q.tt * grid_q.th * grid_q.tw;
+  return attn::run(q, true, &grid_q, k_vis, v_vis, true, &grid_k, k_txt, v_txt, bs, idx, sm_scale, o, lse, err_word,
+                   stream);
+}

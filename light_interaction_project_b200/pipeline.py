@@ -1,0 +1,80 @@
+"""The sparse-attention pipeline shared by the three orchestrators.
+
+Reference stages (``ar_sparse_operation.py:289-362``): allocate tiled Q/K/V +
+pools, copy padded text K/V, tile+pool Q and K/V (Triton), select blocks
+(torch), block-sparse attention on the tiled tensors (Triton), untile. Here:
+
+1. ``li_tile_pool`` (pool only) writes the q and k block means — the tiled
+   copies are never materialised;
+2. ``li_select_blocks`` builds the sorted index list (text blocks first);
+3. ``li_sparse_attn_raster`` reads q, the visual K/V and the text K/V straight
+   from the caller's tensors, 3D block by 3D block, and writes the output in
+   q's raster layout.
+
+Three launches, no host synchronisation, no intermediate tiled tensors.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+from . import kernels as K
+
+
+def latent_grids(q_len: int, k_len: int, latent_hw, tile):
+    """Frame counts and block grids — ``ar_sparse_operation.py:319-327``."""
+    LH, LW = latent_hw
+    HW = LH * LW
+    T_q, T_k = q_len // HW, k_len // HW
+    return T_q, T_k, K.grid_blocks(T_q, LH, LW, tile), K.grid_blocks(T_k, LH, LW, tile)
+
+
+def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode: int, default_tile,
+                   default_metric: str = "cosine", ratio: Optional[float] = None, min_budget: int = 7,
+                   q_block_offset: Optional[int] = None, score_bias: Optional[torch.Tensor] = None,
+                   profile: Optional[dict] = None):
+    LH, LW = latent_hw
+    tile = tuple(int(x) for x in params.get("tile_size", default_tile))
+    text_len = k_txt.shape[2] if k_txt is not None else 0
+    T_q, T_k, gq, gk = latent_grids(q.shape[2], k_vis.shape[2], latent_hw, tile)
+    nq, nk = gq[0] * gq[1] * gq[2], gk[0] * gk[1] * gk[2]
+    if mode == L.SELECT_BIDIR and q_block_offset is None and nq != nk:
+        # generate_prefill_indices broadcasts an [N_k, N_k] neighbour matrix over
+        # [.., N_q, N_k] scores and fails unless N_q == N_k.
+        raise RuntimeError(f"bidirectional block selection needs N_q == N_k (got {nq} and {nk})")
+    if k_vis.dtype != q.dtype:
+        raise TypeError("q and k_vis must share a dtype")
+
+    def mark(name):
+        if profile is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            profile[name] = ev
+
+    mark("prep_start")
+    q_pool = K.pool_blocks(q, T_q, LH, LW, tile)
+    k_pool = K.pool_blocks(k_vis, T_k, LH, LW, tile)
+    mark("prep_end")
+    p = K.select_params(mode, params.get("sim_metric", default_metric), tile, gq, gk, text_len,
+                        recent_protect=params.get("recent_protect", 0),
+                        topk_ratio=params.get("topk_ratio", 1.0) if ratio is None else ratio,
+                        min_budget=min_budget, q_block_offset=q_block_offset or 0)
+    mark("index_start")
+    idx, cnt = K.select_blocks(q_pool, k_pool, p, score_bias=score_bias)
+    mark("index_end")
+    mark("attn_start")
+    out = K.sparse_attn_raster(q, L.grid3d(T_q, LH, LW, tile), k_txt, v_txt, k_vis, v_vis,
+                               L.grid3d(T_k, LH, LW, tile), idx, cnt, sm_scale=1.0 / math.sqrt(q.shape[-1]))
+    mark("attn_end")
+    return out
+
+
+def dense_attention(q, k, v):
+    """The reference's dense branch (``F.scaled_dot_product_attention``), kept
+    where its orchestrators fall back to it (untileable query length; HY
+    prefill warm-up chunks)."""
+    return torch.nn.functional.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)

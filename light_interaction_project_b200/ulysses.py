@@ -1,0 +1,169 @@
+"""Head-sharded multi-GPU step: Ulysses sequence<->head all-to-all around the
+block-sparse attention.
+
+The upstream attention processors shard the sequence across ranks and, before
+attention, re-lay q/k/v from ``[B, S/P, H, D]`` to ``[B, S, H/P, D]`` with
+``all_to_all_4D(x, scatter_dim=2, gather_dim=1)``; after attention the output
+goes back with ``all_to_all_4D(o, scatter_dim=1, gather_dim=2)``
+(hy-worldplay/patches/0001-integrate-acceleration.patch:646-654,744-745).
+Selection and attention are independent per (b, h), so with heads split the
+sparse op itself needs no communication.
+
+Here the exchange is one NCCL ``all_to_all_single`` per direction over the
+q/k/v stack (one collective for all three), on the current stream. The
+attention reads q straight from the all-to-all output through a strided view
+(no re-layout copy); K/V of the current chunk are written once into the tail
+of each layer's resident K/V buffer (the reference concatenates the cached
+context with the new chunk, ``hy patch:681-691``, which copies all of it).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import bi_sparse_operation as mg
+from . import kernels as K
+
+
+def seq_to_head(x: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """``[N, B, s, H, D]`` (N stacked tensors, s = S/P local tokens) ->
+    ``[P*s, N, B, H/P, D]`` (all tokens, this rank's heads), contiguous."""
+    N, B, s, H, D = x.shape
+    if world == 1:
+        return x.permute(2, 0, 1, 3, 4).contiguous()
+    hl = H // world
+    send = x.reshape(N, B, s, world, hl, D).permute(3, 2, 0, 1, 4, 5).contiguous()  # [P, s, N, B, hl, D]
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.reshape(world * s, N, B, hl, D)
+
+
+def head_to_seq(o: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """``[B, H/P, S, D]`` (this rank's heads, all tokens) -> ``[B, S/P, H, D]``."""
+    B, hl, S, D = o.shape
+    if world == 1:
+        return o.permute(0, 2, 1, 3)
+    s = S // world
+    send = o.permute(2, 0, 1, 3).reshape(world, s, B, hl, D).contiguous()  # [P, s, B, hl, D]
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.permute(2, 1, 0, 3, 4).reshape(B, s, world * hl, D)
+
+
+@dataclass
+class StackConfig:
+    layers: int = 30
+    heads: int = 24
+    head_dim: int = 128
+    hidden: int = 3072
+    latent_hw: tuple = (30, 52)
+    query_frames: int = 4
+    memory_frames: int = 64
+    tile: tuple = (4, 4, 8)
+    keep_ratio: float = 0.25
+    metric: str = "cosine"
+    batch: int = 1
+
+    @property
+    def frame_tokens(self):
+        return self.latent_hw[0] * self.latent_hw[1]
+
+    @property
+    def q_tokens(self):
+        return self.query_frames * self.frame_tokens
+
+    @property
+    def kv_frames(self):
+        return self.memory_frames + self.query_frames
+
+    def blocks(self):
+        LH, LW = self.latent_hw
+        nq = K.grid_blocks(self.query_frames, LH, LW, self.tile)
+        nk = K.grid_blocks(self.kv_frames, LH, LW, self.tile)
+        return nq[0] * nq[1] * nq[2], nk[0] * nk[1] * nk[2]
+
+    def budget(self):
+        _, nk = self.blocks()
+        return min(max(int(nk * self.keep_ratio), 7), nk)
+
+    def attention_flops(self, heads: Optional[int] = None) -> float:
+        """Executed FLOPs of one attention call over the padded tiled layout."""
+        nq, _ = self.blocks()
+        bs = self.tile[0] * self.tile[1] * self.tile[2]
+        h = self.heads if heads is None else heads
+        return 4.0 * self.batch * h * nq * bs * self.budget() * bs * self.head_dim
+
+
+class HeadShardedStack:
+    """``layers`` attention layers of one query chunk, heads split over ``world``
+    ranks: QKV projection -> all-to-all -> block-sparse attention over the
+    resident (memory + current chunk) K/V -> all-to-all -> O projection."""
+
+    def __init__(self, cfg: StackConfig, rank: int, world: int, device, group=None, seed: int = 0):
+        if cfg.heads % world or cfg.q_tokens % world:
+            raise ValueError("heads and query tokens must divide by the world size")
+        self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
+        self.device = torch.device(device)
+        self.hl = cfg.heads // world
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed + 1000 * rank)
+        std = 1.0 / math.sqrt(cfg.hidden)
+        dt = torch.bfloat16
+        hd = cfg.heads * cfg.head_dim
+        # Same weights on every rank (seeded without the rank).
+        gw = torch.Generator(device=self.device)
+        gw.manual_seed(seed)
+        self.w_qkv = [(torch.randn(cfg.hidden, 3 * hd, generator=gw, device=self.device) * std).to(dt)
+                      for _ in range(cfg.layers)]
+        self.w_o = [(torch.randn(hd, cfg.hidden, generator=gw, device=self.device) * std).to(dt)
+                    for _ in range(cfg.layers)]
+        kv_tokens = cfg.kv_frames * cfg.frame_tokens
+        self.k_buf: List[torch.Tensor] = []
+        self.v_buf: List[torch.Tensor] = []
+        for _ in range(cfg.layers):
+            self.k_buf.append(torch.randn(cfg.batch, self.hl, kv_tokens, cfg.head_dim, generator=g,
+                                          device=self.device).to(dt))
+            self.v_buf.append(torch.randn(cfg.batch, self.hl, kv_tokens, cfg.head_dim, generator=g,
+                                          device=self.device).to(dt))
+        nq, nk = cfg.blocks()
+        self.q_block_offset = nk - nq
+        self.params = {"tile_size": tuple(cfg.tile), "topk_ratio": cfg.keep_ratio, "sim_metric": cfg.metric}
+
+    def local_tokens(self):
+        return self.cfg.q_tokens // self.world
+
+    def make_input(self, seed: int = 7) -> torch.Tensor:
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed + self.rank)
+        return torch.randn(self.cfg.batch, self.local_tokens(), self.cfg.hidden, generator=g,
+                           device=self.device).to(torch.bfloat16)
+
+    def layer(self, i: int, x: torch.Tensor, attn_events=None) -> torch.Tensor:
+        cfg = self.cfg
+        B, s, _ = x.shape
+        qkv = (x.reshape(B * s, cfg.hidden) @ self.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
+        full = seq_to_head(qkv.permute(2, 0, 1, 3, 4), self.world, self.group)   # [S, 3, B, hl, D]
+        S = full.shape[0]
+        q = full[:, 0].permute(1, 2, 0, 3)                                       # [B, hl, S, D] view
+        tail = self.k_buf[i].shape[2] - S
+        self.k_buf[i][:, :, tail:].copy_(full[:, 1].permute(1, 2, 0, 3))
+        self.v_buf[i][:, :, tail:].copy_(full[:, 2].permute(1, 2, 0, 3))
+        if attn_events is not None:
+            attn_events[0].record()
+        o = mg.run_sparse_attention(q, self.k_buf[i], self.v_buf[i], 0, i, cfg.latent_hw, self.params,
+                                    q_block_offset=self.q_block_offset)
+        if attn_events is not None:
+            attn_events[1].record()
+        back = head_to_seq(o, self.world, self.group)                           # [B, s, H, D]
+        out = back.reshape(B * s, cfg.heads * cfg.head_dim) @ self.w_o[i]
+        return x + out.view(B, s, cfg.hidden)
+
+    def step(self, x: torch.Tensor, attn_events=None) -> torch.Tensor:
+        for i in range(self.cfg.layers):
+            x = self.layer(i, x, attn_events[i] if attn_events is not None else None)
+        return x

@@ -61,6 +61,9 @@ def round_to(x, dtype: str) -> np.ndarray:
     x = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
     if dtype == "fp32":
         return x
+    if dtype == "fp16":
+        with np.errstate(over="ignore"):  # overflow to inf, as the GPU conversion does
+            return x.astype(np.float16).astype(np.float32)
     if dtype != "bf16":
         raise ValueError(f"unsupported dtype {dtype}")
     u = x.view(np.uint32).astype(np.uint64)
@@ -78,12 +81,18 @@ def bf16_bits(x: np.ndarray) -> np.ndarray:
 
 
 def radix_key(x: np.ndarray, dtype: str) -> np.ndarray:
-    """Order-preserving unsigned key (torch's TopKTypeConfig transform)."""
-    if dtype == "bf16":
-        b = bf16_bits(x).astype(np.uint32)
-        return np.where(b & 0x8000, b ^ 0xFFFF, b ^ 0x8000).astype(np.uint64)
-    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    return np.where(b & 0x80000000, b ^ 0xFFFFFFFF, b ^ 0x80000000).astype(np.uint64)
+    """Order-preserving unsigned key (torch's TopKTypeConfig transform; NaN highest)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if dtype in ("bf16", "fp16"):
+        if dtype == "bf16":
+            b = bf16_bits(x).astype(np.uint32)
+        else:
+            b = x.astype(np.float16).view(np.uint16).astype(np.uint32)
+        key = np.where(b & 0x8000, b ^ 0xFFFF, b ^ 0x8000)
+        return np.where(np.isnan(x), 0xFFFF, key).astype(np.uint64)
+    b = x.view(np.uint32).astype(np.uint64)
+    key = np.where(b & 0x80000000, b ^ 0xFFFFFFFF, b ^ 0x80000000)
+    return np.where(np.isnan(x), 0xFFFFFFFF, key).astype(np.uint64)
 
 
 # ----------------------------------------------------------------------------

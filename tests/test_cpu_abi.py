@@ -1,0 +1,99 @@
+"""CPU-only checks of the C ABI library and the host-side logic (no GPU calls)."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from light_interaction_project_b200 import _lib as L
+from light_interaction_project_b200 import build_lib
+from light_interaction_project_b200 import kernels as K
+from oracle import li_oracle as O
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "li_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_lib.build()
+    return L.load()
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^(?:li_status|const char\*)\s+(li_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_every_bound_symbol():
+    assert declared_symbols() == sorted(L.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.li_version().decode().startswith("li_b200")
+
+
+@pytest.mark.parametrize("nk", [0, 1, 5, 63, 64, 192, 256, 280, 952, 1024])
+@pytest.mark.parametrize("ratio", [0.0, 0.1, 0.175, 0.25, 0.3, 0.5, 1.0])
+@pytest.mark.parametrize("rp", [0, 1, 2, 4, 9])
+def test_decode_budget_matches_reference_formula(lib, nk, ratio, rp):
+    tile, gq = (4, 8, 4), (1, 4, 4)
+    p = K.select_params(L.SELECT_DECODE, "cosine", tile, gq, (8, 4, 4), 5, rp, ratio)
+    ntxt, k = K.select_budget(p, 16, nk)
+    n_prot, ref_k = O.decode_budget(nk, tile, gq, dict(recent_protect=rp, topk_ratio=ratio))
+    assert (ntxt, k) == (1, ref_k)
+
+
+@pytest.mark.parametrize("nk", [0, 1, 6, 7, 8, 23, 280, 1120])
+@pytest.mark.parametrize("ratio", [0.0, 0.1, 0.25, 0.3, 0.5, 1.0])
+def test_bidir_budget_matches_reference_formula(lib, nk, ratio):
+    p = K.select_params(L.SELECT_BIDIR, "cosine", (4, 4, 8), (1, 1, 1), (1, 1, 1), 130, 0, ratio)
+    ntxt, k = K.select_budget(p, nk, nk)
+    assert (ntxt, k) == (2, O.prefill_budget(nk, ratio))
+
+
+def test_entry_points_validate_before_launch(lib):
+    """Null or inconsistent arguments come back as status codes; nothing launches."""
+    assert lib.li_tile_pool(None, None, None, L.grid3d(1, 1, 1, (1, 1, 1)), None, None, 0, None, 0, None) == L.LI_ERR_INVALID_ARG
+    assert "src0" in L.last_error()
+    v = L.View4()
+    v.data = 16
+    for i, (s, st) in enumerate(zip((1, 1, 64, 128), (8192, 8192, 128, 1))):
+        v.shape[i], v.stride[i] = s, st
+    v.dtype = L.DTYPE_BF16
+    bad_grid = L.grid3d(1, 8, 8, (1, 8, 0))
+    assert lib.li_tile_pool(ctypes.byref(v), None, None, bad_grid, None, None, 0, None, 0, None) == L.LI_ERR_SHAPE
+    v.dtype = 7
+    assert lib.li_tile_pool(ctypes.byref(v), None, None, L.grid3d(1, 8, 8, (1, 8, 8)), None, None, 0, None, 0,
+                            None) == L.LI_ERR_INVALID_ARG
+    # Attention: fp32 operands are not built (the Python layer casts them).
+    v.dtype = L.DTYPE_FP32
+    iv = L.IndexView()
+    st = lib.li_sparse_attn_tiled(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(iv), 128, 1.0,
+                                  ctypes.byref(v), None, None, None)
+    assert st == L.LI_ERR_UNSUPPORTED
+    v.dtype = L.DTYPE_BF16
+    st = lib.li_sparse_attn_tiled(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(iv), 96, 1.0,
+                                  ctypes.byref(v), None, None, None)
+    assert st == L.LI_ERR_UNSUPPORTED
+    with pytest.raises(NotImplementedError):
+        L.check(st, "attn")
+
+
+def test_rank_blocks_rejects_k_out_of_range(lib):
+    v = L.View4()
+    v.data = 256
+    for i, (s, st) in enumerate(zip((1, 1, 4, 10), (40, 40, 10, 1))):
+        v.shape[i], v.stride[i] = s, st
+    v.dtype = L.DTYPE_FP32
+    iv = L.IndexView()
+    assert lib.li_rank_blocks(ctypes.byref(v), L.DTYPE_BF16, 11, 0, 128, ctypes.byref(iv), None) == L.LI_ERR_OUT_OF_BOUNDS
+
+
+def test_tensor_wrappers_refuse_cpu_tensors():
+    import torch
+    with pytest.raises(ValueError, match="CUDA"):
+        L.view4(torch.zeros(1, 1, 1, 8), "x")

@@ -1,0 +1,215 @@
+"""GPU parity of the tcgen05 block-sparse attention against the fp32 oracle.
+
+Tolerance (bf16/fp16 outputs): max-abs 2e-2 and mean-abs 2e-3 against the
+oracle's fp32 attention over the same selected blocks.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from golden_util import list_cases, load_case, rebuild_inputs
+from gpu_util import TORCH_DT, assert_close_bf16, dev, rand, to_gpu, to_np
+from light_interaction_project_b200 import _lib as L
+from light_interaction_project_b200 import ar_sparse_operation as ar
+from light_interaction_project_b200 import bi_sparse_operation as mg
+from light_interaction_project_b200 import bi_sparse_operation_for_KV_cache as hyp
+from light_interaction_project_b200 import kernels as K
+from light_interaction_project_b200.longcat_kernel import longcat_flash_attn
+from oracle import li_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _random_lists(rng, B, H, nq, nkb, S, vary=True):
+    idx = np.zeros((B, H, nq, S), np.int32)
+    cnt = np.full((B, H, nq), S, np.int32)
+    for b in range(B):
+        for h in range(H):
+            for i in range(nq):
+                c = int(rng.integers(0, S + 1)) if vary else S
+                sel = np.sort(rng.choice(nkb, size=S, replace=False))
+                idx[b, h, i] = sel
+                cnt[b, h, i] = c
+    return idx, cnt
+
+
+@pytest.mark.parametrize("D,bs", [(128, 128), (128, 64), (64, 128), (64, 64)])
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_tiled_attention_vs_oracle(cuda_ok, D, bs, dtype):
+    B, H, nq, nkb, S = 1, 3, 5, 9, 4
+    q, tq = rand((B, H, nq * bs, D), 501, dtype)
+    k, tk = rand((B, H, nkb * bs, D), 502, dtype)
+    v, tv = rand((B, H, nkb * bs, D), 503, dtype)
+    idx, cnt = _random_lists(np.random.default_rng(0), B, H, nq, nkb, S)
+    cnt[0, 0, 0] = 0  # an empty list gives a zero output row block
+    ti, tc = torch.from_numpy(idx).to(dev()), torch.from_numpy(cnt).to(dev())
+    out = longcat_flash_attn(tq, tk, tv, ti, tc, logical_block_size=bs)
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    ref, _ = O.sparse_attention_tiled(q.reshape(B, H, nq, bs, D), k.reshape(B, H, nkb, bs, D),
+                                      v.reshape(B, H, nkb, bs, D), idx, cnt, p_dtype=dtype if dtype == "bf16" else None)
+    assert_close_bf16(to_np(out), ref.reshape(B, H, nq * bs, D), what=f"D={D} bs={bs} {dtype}")
+    assert (to_np(out)[0, 0, :bs] == 0).all()
+
+
+def test_tiled_attention_long_lists_and_lse(cuda_ok):
+    """Many blocks per row (online-softmax rescaling exercised) plus the LSE output."""
+    B, H, D, bs, nq, nkb, S = 2, 2, 128, 128, 3, 40, 33
+    q, tq = rand((B, H, nq * bs, D), 601, "bf16", scale=2.0)
+    k, tk = rand((B, H, nkb * bs, D), 602, "bf16", scale=2.0)
+    v, tv = rand((B, H, nkb * bs, D), 603, "bf16")
+    idx, cnt = _random_lists(np.random.default_rng(1), B, H, nq, nkb, S, vary=False)
+    out, lse = K.sparse_attn_tiled(tq, tk, tv, torch.from_numpy(idx).to(dev()), torch.from_numpy(cnt).to(dev()),
+                                   bs, return_lse=True)
+    torch.cuda.synchronize()
+    ref, ref_lse = O.sparse_attention_tiled(q.reshape(B, H, nq, bs, D), k.reshape(B, H, nkb, bs, D),
+                                            v.reshape(B, H, nkb, bs, D), idx, cnt, p_dtype="bf16")
+    assert_close_bf16(to_np(out), ref.reshape(B, H, nq * bs, D))
+    np.testing.assert_allclose(to_np(lse), ref_lse.reshape(B, H, -1), atol=2e-3, rtol=1e-4)
+
+
+def test_tiled_attention_rejects_like_reference(cuda_ok):
+    t = torch.zeros((1, 1, 256, 128), device=dev(), dtype=torch.bfloat16)
+    k = torch.zeros((1, 1, 200, 128), device=dev(), dtype=torch.bfloat16)
+    i = torch.zeros((1, 1, 2, 1), device=dev(), dtype=torch.int32)
+    c = torch.ones((1, 1, 2), device=dev(), dtype=torch.int32)
+    with pytest.raises(ValueError, match="divisible"):
+        longcat_flash_attn(t, k, k, i, c)
+    with pytest.raises(ValueError, match="out of bounds"):
+        longcat_flash_attn(t, t, t, i + 2, c)
+
+
+def test_out_of_range_index_flagged_on_device(cuda_ok):
+    """With the host check skipped, the kernel bounds-checks every block id."""
+    B, H, D, bs = 1, 1, 128, 128
+    _, t = rand((B, H, 2 * bs, D), 1, "bf16")
+    i = torch.tensor([[[[0, 5]], [[1, 1]]]], device=dev(), dtype=torch.int32).reshape(1, 1, 2, 2)
+    c = torch.full((1, 1, 2), 2, device=dev(), dtype=torch.int32)
+    longcat_flash_attn(t, t, t, i, c, validate=False)
+    torch.cuda.synchronize()
+    assert K.device_errors() & L.LI_DEVERR_BAD_INDEX
+
+
+ORCH_CASES = [
+    # (kind, B, H, D, LH, LW, Fq, Fk, text_len, params, dtype)
+    ("hy_decode", 1, 2, 128, 30, 52, 4, 16, 0,
+     dict(tile_size=(1, 8, 16), topk_ratio=0.25, recent_protect=4, sim_metric="scaled_dot_product"), "bf16"),
+    ("hy_decode", 2, 2, 128, 12, 20, 2, 6, 37,
+     dict(tile_size=(4, 8, 4), topk_ratio=0.175, recent_protect=4, sim_metric="scaled_dot_product"), "bf16"),
+    ("hy_prefill", 1, 2, 128, 12, 16, 8, 8, 7,
+     dict(tile_size=(4, 8, 4), topk_ratio=0.3, sim_metric="scaled_dot_product"), "bf16"),
+    ("mg", 1, 3, 128, 10, 20, 6, 6, 0, dict(tile_size=(4, 4, 8), topk_ratio=0.3, sim_metric="cosine"), "bf16"),
+    ("mg", 1, 2, 128, 8, 16, 4, 4, 130, dict(tile_size=(4, 4, 8), topk_ratio=0.3, sim_metric="cosine"), "fp16"),
+    ("hy_decode", 1, 4, 64, 8, 8, 2, 6, 0,
+     dict(tile_size=(2, 4, 8), topk_ratio=0.5, recent_protect=2, sim_metric="scaled_dot_product"), "fp32"),
+]
+
+
+@pytest.mark.parametrize("case", ORCH_CASES)
+def test_orchestrators_vs_oracle(cuda_ok, case):
+    kind, B, H, D, LH, LW, Fq, Fk, tl, params, dtype = case
+    HW = LH * LW
+    q, tq = rand((B, H, Fq * HW, D), 701, dtype)
+    kt, tkt = rand((B, H, tl, D), 702, dtype)
+    vt, tvt = rand((B, H, tl, D), 703, dtype)
+    kv, tkv = rand((B, H, Fk * HW, D), 704, dtype)
+    vv, tvv = rand((B, H, Fk * HW, D), 705, dtype)
+    if kind == "hy_decode":
+        out = ar.run_sparse_attention(tq, tkt, tvt, tkv, tvv, 3, (LH, LW), params)
+        ref, aux = O.run_sparse_attention_hy(q, kt, vt, kv, vv, (LH, LW), params, dtype)
+    elif kind == "hy_prefill":
+        hyp.get_infer_state().current_chunk_index = 4
+        try:
+            out = hyp.run_sparse_prefill_attention(tq, tkt, tvt, tkv, tvv, 3, (LH, LW), params)
+        finally:
+            hyp.get_infer_state().current_chunk_index = 0
+        ref, aux = O.run_sparse_prefill_attention_hy(q, kt, vt, kv, vv, (LH, LW), params, dtype)
+    else:
+        k = np.concatenate([kt, kv], axis=2)
+        v = np.concatenate([vt, vv], axis=2)
+        out = mg.run_sparse_attention(tq, to_gpu(k, dtype), to_gpu(v, dtype), tl, 3, (LH, LW), params)
+        ref, aux = O.run_sparse_attention_mg(q, k, v, tl, (LH, LW), params, dtype)
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    assert out.dtype == TORCH_DT[dtype] and out.shape == tq.shape
+    assert_close_bf16(to_np(out), ref, what=kind)
+
+
+def test_hy_prefill_warmup_chunks_are_dense(cuda_ok):
+    B, H, D, LH, LW, F = 1, 2, 128, 8, 16, 4
+    _, tq = rand((B, H, F * LH * LW, D), 1, "bf16")
+    _, tk = rand((B, H, F * LH * LW, D), 2, "bf16")
+    _, tv = rand((B, H, F * LH * LW, D), 3, "bf16")
+    txt = tk[:, :, :0]
+    out = hyp.run_sparse_prefill_attention(tq, txt, txt, tk, tv, 1, (LH, LW),
+                                           dict(tile_size=(4, 8, 4), topk_ratio=0.3))
+    ref = torch.nn.functional.scaled_dot_product_attention(tq, tk, tv)
+    assert torch.equal(out, ref)
+
+
+def test_hy_transposed_views_and_batch2(cuda_ok):
+    """HY hands over q as ``query.transpose(1, 2)`` of a [B, S, H, D] tensor with
+    B = 2 (plain + ProPE streams): batch and head strides do not merge."""
+    B, S, H, D, LH, LW = 2, 4 * 240, 3, 128, 12, 20
+    qb, tqb = rand((B, S, H, D), 801, "bf16")
+    kv, tkv = rand((B, H, 8 * 240, D), 802, "bf16")
+    vv, tvv = rand((B, H, 8 * 240, D), 803, "bf16")
+    kt, tkt = rand((1, H, 20, D), 804, "bf16")
+    vt, tvt = rand((1, H, 20, D), 805, "bf16")
+    tkt2, tvt2 = tkt.expand(B, H, 20, D), tvt.expand(B, H, 20, D)
+    params = dict(tile_size=(4, 8, 4), topk_ratio=0.175, recent_protect=4, sim_metric="scaled_dot_product")
+    out = ar.run_sparse_attention(tqb.transpose(1, 2), tkt2, tvt2, tkv, tvv, 2, (LH, LW), params)
+    torch.cuda.synchronize()
+    ref, _ = O.run_sparse_attention_hy(qb.transpose(0, 2, 1, 3), np.broadcast_to(kt, (B, H, 20, D)),
+                                       np.broadcast_to(vt, (B, H, 20, D)), kv, vv, (LH, LW), params, "bf16")
+    assert_close_bf16(to_np(out), ref)
+
+
+@pytest.mark.parametrize("name", [c for c in list_cases() if not c.startswith("sel_")])
+def test_reference_fixtures_end_to_end(cuda_ok, name):
+    """Reference inputs through the drop-in orchestrators vs the reference's
+    own output (its Triton kernels, run on CPU when the fixtures were made)."""
+    meta, g = load_case(name)
+    dtype = meta["dtype"]
+    inp = rebuild_inputs(meta)
+    params = dict(meta["params"])
+    params["tile_size"] = tuple(params["tile_size"])
+    LH, LW = meta["LH"], meta["LW"]
+    if meta["kind"] == "mg":
+        out = mg.run_sparse_attention(to_gpu(inp["q"], dtype), to_gpu(inp["k"], dtype), to_gpu(inp["v"], dtype),
+                                      meta["text_len"], 1, (LH, LW), params)
+    elif meta["kind"] == "hy_decode":
+        out = ar.run_sparse_attention(*(to_gpu(inp[x], dtype) for x in ("q", "k_txt", "v_txt", "k_vis", "v_vis")),
+                                      1, (LH, LW), params)
+    else:
+        hyp.get_infer_state().current_chunk_index = 3
+        try:
+            out = hyp.run_sparse_prefill_attention(
+                *(to_gpu(inp[x], dtype) for x in ("q", "k_txt", "v_txt", "k_vis", "v_vis")), 1, (LH, LW), params)
+        finally:
+            hyp.get_infer_state().current_chunk_index = 0
+    torch.cuda.synchronize()
+    got = to_np(out)
+    # Where the reference's CPU top-k kept a different one of two tied blocks the
+    # outputs legitimately differ; compare against the masked reference computed
+    # with our (oracle-equal) indices, and against the reference's own output on
+    # the rows whose selection matches.
+    ref_ours, aux = (O.run_sparse_attention_mg(inp["q"], inp["k"], inp["v"], meta["text_len"], (LH, LW), params, dtype)
+                     if meta["kind"] == "mg" else
+                     (O.run_sparse_attention_hy if meta["kind"] == "hy_decode" else O.run_sparse_prefill_attention_hy)(
+                         inp["q"], inp["k_txt"], inp["v_txt"], inp["k_vis"], inp["v_vis"], (LH, LW), params, dtype))
+    assert_close_bf16(got, ref_ours, what=name)
+    same_rows = (aux["indices"] == g["indices"]).all(-1)
+    tile = params["tile_size"]
+    qtok = O._block_token_index(meta["Fq"], LH, LW, tile)
+    for b, h in np.ndindex(same_rows.shape[:2]):
+        rows = np.concatenate([qtok[i][qtok[i] >= 0] for i in np.nonzero(same_rows[b, h])[0]] or [np.zeros(0, int)])
+        if name.startswith("toy"):
+            ref_rows = g["out_masked"][b, h, rows]   # the reference kernel mis-handles 64-token query blocks
+        else:
+            ref_rows = g["out_ref"][b, h, rows]
+        if rows.size:
+            assert_close_bf16(got[b, h, rows], ref_rows, what=f"{name} b{b} h{h}")
