@@ -292,13 +292,87 @@ def run_gpu(args, cfg, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_gpu_layer(args, rank, world, local_rank):
+    """one Matrix-Game-shaped layer. K/V of 16 retained frames
+    (drawn without replacement from a 64-frame seeded pool) are gathered behind
+    the resident current chunk, then pooling, selection (query-chunk rows of the
+    bidirectional selection) and the sparse attention run through the public
+    ``run_sparse_attention``. Heads are split across ranks (no collective)."""
+    from light_interaction_project_b200 import bi_sparse_operation as mg
+    from light_interaction_project_b200 import kernels as K
+    from light_interaction_project_b200.ulysses import StackConfig
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = StackConfig(layers=1, memory_frames=16, keep_ratio=0.30)
+    H = cfg.heads // world
+    LH, LW = cfg.latent_hw
+    HW = LH * LW
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    pool_frames = 64
+    k_pool = torch.randn(1, H, pool_frames * HW, 128, generator=g, device=dev).to(torch.bfloat16)
+    v_pool = torch.randn(1, H, pool_frames * HW, 128, generator=g, device=dev).to(torch.bfloat16)
+    rng = np.random.default_rng(1234)
+    ids = torch.from_numpy(rng.choice(pool_frames, 16, replace=False).astype(np.int32)).to(dev)
+    kv_tokens = cfg.kv_frames * HW
+    k_buf = torch.randn(1, H, kv_tokens, 128, generator=g, device=dev).to(torch.bfloat16)
+    v_buf = torch.randn(1, H, kv_tokens, 128, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(1, H, cfg.q_tokens, 128, generator=g, device=dev).to(torch.bfloat16)
+    nq, nk = cfg.blocks()
+    params = {"tile_size": cfg.tile, "topk_ratio": cfg.keep_ratio, "sim_metric": cfg.metric}
+
+    def step():
+        K.gather_frames(k_pool, ids, HW, out=k_buf[:, :, :16 * HW])
+        K.gather_frames(v_pool, ids, HW, out=v_buf[:, :, :16 * HW])
+        return mg.run_sparse_attention(q, k_buf, v_buf, 0, 0, cfg.latent_hw, params, q_block_offset=nk - nq)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    # Attention kernel alone.
+    qp = K.pool_blocks(q, cfg.query_frames, LH, LW, cfg.tile)
+    kp = K.pool_blocks(k_buf, cfg.kv_frames, LH, LW, cfg.tile)
+    gq = K.grid_blocks(cfg.query_frames, LH, LW, cfg.tile)
+    gk = K.grid_blocks(cfg.kv_frames, LH, LW, cfg.tile)
+    from light_interaction_project_b200 import _lib as L
+    p = K.select_params(L.SELECT_BIDIR, cfg.metric, cfg.tile, gk, gk, 0, 0, cfg.keep_ratio, 7, nk - nq)
+    idx, cnt = K.select_blocks(qp, kp, p)
+    gq3, gk3 = L.grid3d(cfg.query_frames, LH, LW, cfg.tile), L.grid3d(cfg.kv_frames, LH, LW, cfg.tile)
+    for _ in range(3):
+        K.sparse_attn_raster(q, gq3, None, None, k_buf, v_buf, gk3, idx, cnt)
+    s.record()
+    for _ in range(args.steps):
+        K.sparse_attn_raster(q, gq3, None, None, k_buf, v_buf, gk3, idx, cnt)
+    e.record()
+    torch.cuda.synchronize()
+    attn_ms = s.elapsed_time(e) / args.steps
+    K.raise_device_errors(dev)
+    if rank == 0:
+        fl = cfg.attention_flops(H)
+        burst, sustained, kind = _peaks()
+        print(json.dumps({"metric": METRIC, "workload": "config3_mg_layer", "n_gpus": world,
+                          "value": fl * world / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_call": ms,
+                          "attn_kernel_ms": attn_ms, "attn_kernel_tflops": fl / (attn_ms * 1e-3) / 1e12,
+                          "frac_of_burst": fl / (attn_ms * 1e-3) / 1e12 / burst, "peak_kind": kind,
+                          "q_blocks": nq, "k_blocks": nk, "selected": cfg.budget(), "clocks": clk.summary()}),
+              flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack"])
+    ap.add_argument("--workload", default="stack", choices=["stack", "mg_layer"])
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--warmup-ref", type=int, default=0)
     args = ap.parse_args()
@@ -309,6 +383,9 @@ def main():
     cfg = StackConfig(layers=args.layers)
     if args.impl == "reference":
         run_reference(args, cfg, rank, world)
+        return
+    if args.workload == "mg_layer":
+        run_gpu_layer(args, rank, world, local_rank)
         return
     if world > 1:
         import datetime

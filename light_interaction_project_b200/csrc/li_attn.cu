@@ -42,10 +42,11 @@ namespace li {
 namespace attn {
 
 constexpr int kMaxMaps = 4;
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;  // 8 softmax warps + 2 MMA warps + TMA warp
+constexpr int kWarpMMA0 = 8, kWarpMMA1 = 9, kWarpTMA = 10;
 constexpr uint64_t kTimeoutNs = 1000000000ull;  // 1 s per wait
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0, kColO = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 256;  // S_0, S_1 at 0 and 128; O_0, O_1 at 256 and 384
 
 struct __align__(64) Params {
   CUtensorMap q_map[kMaxMaps];
@@ -226,14 +227,17 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool f16, bool b_
 template <int D, int BS>
 struct Smem {
   static constexpr int kHalves = D / 64;
+  static constexpr int kNK = 2, kNV = 2;      // K and V ring stages (slot j % 2 = chain of block j)
   static constexpr int kQHalf = 128 * 128;  // 128 rows of 128 bytes
   static constexpr int kKVHalf = BS * 128;
+  static constexpr int kKVTile = kHalves * kKVHalf;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kHalves * kQHalf;
-  static constexpr int kOffV = kOffK + kHalves * kKVHalf;
-  static constexpr int kOffBar = kOffV + kHalves * kKVHalf;
-  static constexpr int kBytes = kOffBar + 128 + 1024;  // + alignment slack
-  static constexpr uint32_t kTileBytes = (uint32_t)kHalves * BS * 128;
+  static constexpr int kOffV = kOffK + kNK * kKVTile;
+  static constexpr int kOffX = kOffV + kNV * kKVTile;     // per-row (m, l) of both chains
+  static constexpr int kOffBar = kOffX + 2 * 2 * 128 * 4;
+  static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
+  static constexpr uint32_t kTileBytes = (uint32_t)kKVTile;
 };
 
 __device__ __forceinline__ void block_coords(int raster, int blk, int bsz, int nh, int nw, int tt, int th, int tw,
@@ -248,8 +252,15 @@ __device__ __forceinline__ void block_coords(int raster, int blk, int bsz, int n
   c[4] = w;
 }
 
+// Named barrier over one chain's 4 softmax warps and its MMA warp. Every
+// participant executes it exactly once per block of the chain (work is
+// skipped, never the barrier, after an abort), so counts always match.
+__device__ __forceinline__ void chain_sync(int chain) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + chain), "r"(160) : "memory");
+}
+
 template <int D, int BS, bool F16>
-__global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ Params p) {
   using L = Smem<D, BS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -261,24 +272,38 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_cons
   const int mi = p.per_batch ? bl : 0;
   const int wc = p.per_batch ? h : b * p.H + h;
 
-  const uint32_t bar_q = sb + L::kOffBar, bar_kf = bar_q + 8, bar_ke = bar_q + 16, bar_vf = bar_q + 24,
-                 bar_ve = bar_q + 32, bar_s = bar_q + 40, bar_p = bar_q + 48, bar_o = bar_q + 56,
-                 bar_fin = bar_q + 64;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffBar + 72);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffBar + 76);
+  // Barriers: q | k_full[2] k_empty[2] | v_full[2] v_empty[2] | s_full[2] | o_full[2] | xs | st
+  const uint32_t bar0 = sb + L::kOffBar;
+  const uint32_t bar_q = bar0;
+  auto bar_kf = [&](int s) { return bar0 + 8 + 8 * s; };
+  auto bar_ke = [&](int s) { return bar0 + 24 + 8 * s; };
+  auto bar_vf = [&](int s) { return bar0 + 40 + 8 * s; };
+  auto bar_ve = [&](int s) { return bar0 + 56 + 8 * s; };
+  auto bar_s = [&](int c) { return bar0 + 72 + 8 * c; };
+  auto bar_o = [&](int c) { return bar0 + 88 + 8 * c; };
+  const uint32_t bar_xs = bar0 + 104, bar_st = bar0 + 112;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffBar + 160);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffBar + 164);
+  float* xm = reinterpret_cast<float*>(smem + L::kOffX);   // [2 chains][128] row max
+  float* xl = xm + 2 * 128;                                 // [2 chains][128] row sum
 
   const int S_raw = p.cnt[b * p.c_b + h * p.c_h + (int64_t)qi * p.c_q];
   const int S = S_raw < 0 ? 0 : (S_raw > p.smax ? p.smax : S_raw);
   if (S != S_raw && threadIdx.x == 0 && p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
   const int32_t* irow = p.idx + b * p.i_b + h * p.i_h + (int64_t)qi * p.i_q;
+  const int n_chain[2] = {(S + 1) / 2, S / 2};  // blocks of chain 0 (even j) and chain 1 (odd j)
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q, 1); mbar_init(bar_kf, 1); mbar_init(bar_ke, 1); mbar_init(bar_vf, 1);
-    mbar_init(bar_ve, 1); mbar_init(bar_s, 1); mbar_init(bar_p, 4); mbar_init(bar_o, 1); mbar_init(bar_fin, 1);
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_kf(s), 1); mbar_init(bar_ke(s), 1); mbar_init(bar_vf(s), 1); mbar_init(bar_ve(s), 1);
+      mbar_init(bar_s(s), 1); mbar_init(bar_o(s), 1);
+    }
+    mbar_init(bar_xs, 8); mbar_init(bar_st, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(smem_u32(smem + L::kOffBar + 72), kTmemCols);
+  if (warp == kWarpMMA0) tmem_alloc(smem_u32(smem + L::kOffBar + 160), kTmemCols);
   if (BS < 128 && warp < 4) {
     // Query rows past the block are zero so the padded MMA rows stay finite.
     for (int hf = 0; hf < L::kHalves; ++hf) {
@@ -292,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kWarpTMA) {
     // ------------------------------ producer ------------------------------
     if (lane == 0 && S > 0) {
       int c[5];
@@ -303,8 +328,10 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_cons
         tma_load_5d(sb + L::kOffQ + hf * L::kQHalf, &p.q_map[mi], c, bar_q);
       }
       int issued_k = 0, issued_v = 0;
+      int nxt = irow[0];
       for (int j = 0; j < S; ++j) {
-        int blk = irow[(int64_t)j * p.i_s];
+        int blk = nxt;
+        if (j + 1 < S) nxt = irow[(int64_t)(j + 1) * p.i_s];
         if (blk < 0 || blk >= p.n_kv) {
           if (p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
           blk = 0;
@@ -319,158 +346,200 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_cons
                        wc, c);
           km = &p.k_map[mi]; vm = &p.v_map[mi];
         }
-        if (j > 0 && !mbar_wait(bar_ke, (j - 1) & 1, abort_flag, p.err)) break;
-        mbar_expect_tx(bar_kf, L::kTileBytes);
+        const int ks = j % L::kNK, vs = j % L::kNV;
+        if (j >= L::kNK && !mbar_wait(bar_ke(ks), ((j / L::kNK) - 1) & 1, abort_flag, p.err)) break;
+        mbar_expect_tx(bar_kf(ks), L::kTileBytes);
         for (int hf = 0; hf < L::kHalves; ++hf) {
           c[0] = 64 * hf;
-          tma_load_5d(sb + L::kOffK + hf * L::kKVHalf, km, c, bar_kf);
+          tma_load_5d(sb + L::kOffK + ks * L::kKVTile + hf * L::kKVHalf, km, c, bar_kf(ks));
         }
         issued_k = j + 1;
-        if (j > 0 && !mbar_wait(bar_ve, (j - 1) & 1, abort_flag, p.err)) break;
-        mbar_expect_tx(bar_vf, L::kTileBytes);
+        if (j >= L::kNV && !mbar_wait(bar_ve(vs), ((j / L::kNV) - 1) & 1, abort_flag, p.err)) break;
+        mbar_expect_tx(bar_vf(vs), L::kTileBytes);
         for (int hf = 0; hf < L::kHalves; ++hf) {
           c[0] = 64 * hf;
-          tma_load_5d(sb + L::kOffV + hf * L::kKVHalf, vm, c, bar_vf);
+          tma_load_5d(sb + L::kOffV + vs * L::kKVTile + hf * L::kKVHalf, vm, c, bar_vf(vs));
         }
         issued_v = j + 1;
       }
       if (*abort_flag) {
         // Drain this CTA's own loads before shared memory is released.
         mbar_wait(bar_q, 0, abort_flag, nullptr, false);
-        if (issued_k) mbar_wait(bar_kf, (issued_k - 1) & 1, abort_flag, nullptr, false);
-        if (issued_v) mbar_wait(bar_vf, (issued_v - 1) & 1, abort_flag, nullptr, false);
+        for (int j = issued_k - L::kNK; j < issued_k; ++j)
+          if (j >= 0) mbar_wait(bar_kf(j % L::kNK), (j / L::kNK) & 1, abort_flag, nullptr, false);
+        for (int j = issued_v - L::kNV; j < issued_v; ++j)
+          if (j >= 0) mbar_wait(bar_vf(j % L::kNV), (j / L::kNV) & 1, abort_flag, nullptr, false);
       }
     }
-  } else if (warp == 5) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0 && S > 0) {
-      constexpr uint32_t idS = idesc_f16(128, BS, F16, false);
-      constexpr uint32_t idPV = idesc_f16(128, D, F16, true);
-      bool issued = false;
-      if (mbar_wait(bar_q, 0, abort_flag, p.err)) {
-        tc_fence_after();
-        for (int j = 0; j < S; ++j) {
-          if (!mbar_wait(bar_kf, j & 1, abort_flag, p.err)) break;
-          tc_fence_after();
+  } else if (warp == kWarpMMA0 || warp == kWarpMMA1) {
+    // --------------------- MMA issuer of chain w ----------------------------
+    // Chain w owns key blocks j = w, w+2, ...: S_j = Q K_j^T into TMEM S_w, then
+    // (after the chain's softmax) O_w += P_j V_j. One lane issues; MMAs of one
+    // thread run in order, so S_{j+2} (issued after PV_j) never overwrites P_j
+    // before PV_j has read it, and s_full for S_j also covers PV_{j-2}.
+    const int w = warp - kWarpMMA0;
+    const int nb = n_chain[w];
+    constexpr uint32_t idS = idesc_f16(128, BS, F16, false);
+    constexpr uint32_t idPV = idesc_f16(128, D, F16, true);
+    const uint32_t tS = tmem + kColS + (uint32_t)w * 128, tO = tmem + kColO + (uint32_t)w * 128;
+    auto issue_s = [&](int j) {
+      const int ks = j % L::kNK;
+      if (!mbar_wait(bar_kf(ks), (j / L::kNK) & 1, abort_flag, p.err)) return;
+      tc_fence_after();
+      const uint32_t kbase = sb + L::kOffK + ks * L::kKVTile;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t ad = sdesc(sb + L::kOffQ + (kk >> 2) * L::kQHalf + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc(sb + L::kOffK + (kk >> 2) * L::kKVHalf + (kk & 3) * 32, 16, 1024);
-            mma_ss(tmem + kColS, ad, bd, idS, kk > 0 ? 1u : 0u);
-          }
-          issued = true;
-          mma_commit(bar_ke);
-          mma_commit(bar_s);
-          if (!mbar_wait(bar_p, j & 1, abort_flag, p.err)) break;
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint64_t ad = sdesc(sb + L::kOffQ + (kk >> 2) * L::kQHalf + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = sdesc(kbase + (kk >> 2) * L::kKVHalf + (kk & 3) * 32, 16, 1024);
+        mma_ss(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
+      }
+      mma_commit(bar_ke(ks));
+      mma_commit(bar_s(w));
+    };
+    if (lane == 0 && nb > 0 && mbar_wait(bar_q, 0, abort_flag, p.err)) {
+      tc_fence_after();
+      issue_s(w);
+    }
+    for (int i = 0; i < nb; ++i) {
+      const int j = w + 2 * i;
+      chain_sync(w);  // softmax of block j has written P_j (or skipped after an abort)
+      if (lane == 0 && !*abort_flag) {
+        tc_fence_after();
+        const int vs = j % L::kNV;
+        if (mbar_wait(bar_vf(vs), (j / L::kNV) & 1, abort_flag, p.err)) {
           tc_fence_after();
-          if (!mbar_wait(bar_vf, j & 1, abort_flag, p.err)) break;
-          tc_fence_after();
+          const uint32_t vbase = sb + L::kOffV + vs * L::kKVTile;
 #pragma unroll
           for (int kk = 0; kk < BS / 16; ++kk) {
-            const uint64_t bd = sdesc(sb + L::kOffV + kk * 2048, L::kKVHalf, 1024);
-            mma_ts(tmem + kColO, tmem + kColS + kk * 8, bd, idPV, (j > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t bd = sdesc(vbase + kk * 2048, L::kKVHalf, 1024);
+            mma_ts(tO, tS + kk * 8, bd, idPV, (i > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(bar_ve);
-          mma_commit(bar_o);
+          mma_commit(bar_ve(vs));
+          if (i + 1 < nb) issue_s(j + 2);
         }
       }
-      if (issued) {
-        // All MMAs of this CTA complete before TMEM is released.
-        mma_commit(bar_fin);
-        mbar_wait(bar_fin, 0, abort_flag, p.err, false);
-      }
+      __syncwarp();
+    }
+    if (lane == 0 && nb > 0) {
+      // Every MMA of this chain completes before O_w is read and TMEM is freed.
+      mma_commit(bar_o(w));
+      mbar_wait(bar_o(w), 0, abort_flag, p.err, false);
     }
   } else {
-    // ------------------------ softmax + epilogue ---------------------------
-    const int row = threadIdx.x;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_base + kColS, tO = tmem + lane_base + kColO;
+    // --------------------- softmax of chain w + epilogue -----------------------
+    // Thread (warp, lane) owns row = (warp & 3) * 32 + lane = TMEM lane.
+    const int w = warp >> 2;
+    const int nb = n_chain[w];
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + kColS + (uint32_t)w * 128;
+    const uint32_t tO = tmem + lane_base + kColO + (uint32_t)w * 128;
     const float c2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < S && ok; ++j) {
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s, j & 1, abort_flag, p.err));
-      if (!ok) break;
-      tc_fence_after();
-      float mx = -INFINITY;
-#pragma unroll
-      for (int cc = 0; cc < BS / 32; ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tS + cc * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
-      }
-      const float m_new = fmaxf(m, mx * c2);
-      const bool need = (j > 0) && (m_new - m > 8.0f);
-      float alpha = 1.f;
-      if (j == 0) {
-        m = m_new;
-      } else if (need) {
-        alpha = ex2(m - m_new);
-        m = m_new;
-      }
-      if (__any_sync(0xFFFFFFFFu, need)) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o, (j - 1) & 1, abort_flag, p.err));
-        if (!ok) break;
+    for (int i = 0; i < nb; ++i) {
+      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s(w), i & 1, abort_flag, p.err));
+      if (ok) {
         tc_fence_after();
+        uint32_t r[BS / 32][32];
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tO + cc * 32, r);
-          tmem_wait_ld();
+        for (int cc = 0; cc < BS / 32; ++cc) tmem_ld32(tS + cc * 32, r[cc]);
+        tmem_wait_ld();
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-          tmem_st32(tO + cc * 32, r);
+        for (int cc = 0; cc < BS / 32; ++cc)
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            mx0 = fmaxf(mx0, __uint_as_float(r[cc][e]));
+            mx1 = fmaxf(mx1, __uint_as_float(r[cc][e + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(r[cc][e + 2]));
+            mx3 = fmaxf(mx3, __uint_as_float(r[cc][e + 3]));
+          }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float m_new = fmaxf(m, mx * c2);
+        // Lazy correction: move the reference max only when it grows by more
+        // than 8 (log2 units); P <= 2^8 otherwise, and O/l stays exact.
+        const bool need = (i > 0) && (m_new - m > 8.0f);
+        const float alpha = need ? ex2(m - m_new) : 1.f;
+        if (i == 0 || need) m = m_new;
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < BS / 32; ++cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const float p0 = ex2(fmaf(__uint_as_float(r[cc][2 * e]), c2, -m));
+            const float p1 = ex2(fmaf(__uint_as_float(r[cc][2 * e + 1]), c2, -m));
+            const float p2 = ex2(fmaf(__uint_as_float(r[cc][2 * e + 2]), c2, -m));
+            const float p3 = ex2(fmaf(__uint_as_float(r[cc][2 * e + 3]), c2, -m));
+            l0 += p0;
+            l1 += p1;
+            l2 += p2;
+            l3 += p3;
+            pk[e] = pack2<F16>(p0, p1);
+            pk[e + 1] = pack2<F16>(p2, p3);
+          }
+          tmem_st16(tS + cc * 16, pk);
+        }
+        l = l * alpha + ((l0 + l1) + (l2 + l3));
+        // O_w rescale (its last PV completed before s_full of this block fired;
+        // PV_j is only issued after the chain barrier below).
+        if (__any_sync(0xFFFFFFFFu, need)) {
+#pragma unroll
+          for (int cc = 0; cc < D / 32; ++cc) {
+            uint32_t o[32];
+            tmem_ld32(tO + cc * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + cc * 32, o);
+          }
         }
         tmem_wait_st();
       }
-      l *= alpha;
+      tc_fence_before();
+      chain_sync(w);  // P_j is in TMEM: the chain's MMA warp may issue PV_j
+    }
+    // ---- epilogue: merge the two chains, O = (a0 O_0 + a1 O_1) / (a0 l0 + a1 l1)
+    if (ok && nb > 0) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o(w), 0, abort_flag, p.err));
+    xm[w * 128 + row] = m;
+    xl[w * 128 + row] = l;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_xs);
+    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_xs, 0, abort_flag, p.err));
+    if (ok && n_chain[1 - w] > 0)
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o(1 - w), 0, abort_flag, p.err));
+    tc_fence_after();
+    const float m0 = xm[row], m1 = xm[128 + row], l0 = xl[row], l1 = xl[128 + row];
+    const float mm = fmaxf(m0, m1);
+    const float a0 = l0 > 0.f ? ex2(m0 - mm) : 0.f, a1 = l1 > 0.f ? ex2(m1 - mm) : 0.f;
+    const float lt = a0 * l0 + a1 * l1;
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    const bool store = ok && !*abort_flag;
+    if (store) {
+      uint8_t* stage = smem + L::kOffQ;
+      constexpr int kOCols = D / 2;  // this warpgroup converts O columns [w*D/2, (w+1)*D/2)
+      const uint32_t o0 = tmem + lane_base + kColO, o1 = tmem + lane_base + kColO + 128;
 #pragma unroll
-      for (int cc = 0; cc < BS / 32; ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tS + cc * 32, r);
+      for (int cc = 0; cc < kOCols / 32; ++cc) {
+        const int col0 = w * kOCols + cc * 32;
+        uint32_t x0[32], x1[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) { x0[e] = 0u; x1[e] = 0u; }
+        if (l0 > 0.f) tmem_ld32(o0 + col0, x0);
+        if (l1 > 0.f) tmem_ld32(o1 + col0, x1);
         tmem_wait_ld();
+        const float s0 = a0 * inv, s1 = a1 * inv;
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(fmaf(__uint_as_float(r[2 * e]), c2, -m));
-          const float p1 = ex2(fmaf(__uint_as_float(r[2 * e + 1]), c2, -m));
-          l += p0 + p1;
-          pk[e] = pack2<F16>(p0, p1);
+          const float v0 = (l0 > 0.f ? __uint_as_float(x0[2 * e]) * s0 : 0.f) +
+                           (l1 > 0.f ? __uint_as_float(x1[2 * e]) * s1 : 0.f);
+          const float v1 = (l0 > 0.f ? __uint_as_float(x0[2 * e + 1]) * s0 : 0.f) +
+                           (l1 > 0.f ? __uint_as_float(x1[2 * e + 1]) * s1 : 0.f);
+          pk[e] = pack2<F16>(v0, v1);
         }
-        tmem_st16(tS + cc * 16, pk);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p);
-    }
-    if (ok && S > 0) {
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o, (S - 1) & 1, abort_flag, p.err));
-      tc_fence_after();
-    }
-    // Named barrier 1: every softmax warp knows whether the CTA aborted.
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    const bool store = ok && !*abort_flag;
-    if (store) {
-      const float inv = S > 0 ? 1.f / l : 0.f;
-      uint8_t* stage = smem + L::kOffQ;
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t r[32];
-        if (S > 0) {
-          tmem_ld32(tO + cc * 32, r);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = 0u;
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          pk[e] = pack2<F16>(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
-        const int col0 = cc * 32, hf = col0 / 64, ch0 = (col0 % 64) / 8;
+        const int hf = col0 / 64, ch0 = (col0 % 64) / 8;
         uint8_t* rowp = stage + hf * L::kQHalf + row * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -480,8 +549,9 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_cons
       }
       fence_proxy_async_smem();
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (store && threadIdx.x == 0) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_st);
+    if (store && threadIdx.x == 0 && mbar_wait(bar_st, 0, abort_flag, p.err) && !*abort_flag) {
       int c[5];
       block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
       for (int hf = 0; hf < L::kHalves; ++hf) {
@@ -490,12 +560,12 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_kernel(const __grid_cons
       }
       tma_store_commit_and_drain();
     }
-    if (store && p.lse && row < BS)
-      p.lse[(int64_t)(b * p.H + h) * p.lse_len + (int64_t)qi * BS + row] = S > 0 ? m + __log2f(l) : -INFINITY;
+    if (store && w == 0 && p.lse && row < BS)
+      p.lse[(int64_t)(b * p.H + h) * p.lse_len + (int64_t)qi * BS + row] = lt > 0.f ? mm + __log2f(lt) : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kWarpMMA0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }

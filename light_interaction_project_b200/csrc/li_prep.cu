@@ -15,7 +15,7 @@ namespace li {
 namespace {
 
 constexpr int kMaxD = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 8;
 
 struct TileArgs {
   const uint8_t* src[2];
@@ -35,13 +35,12 @@ struct TileArgs {
   int32_t H, bs, D, dtype, CH;
 };
 
-__device__ __forceinline__ int64_t token_of(const TileArgs& a, int blk, int r, bool& ok,
-                                            bool& bad_frame) {
+// Raster token of row r of block `blk` (-1: padding or a rejected frame id).
+__device__ __forceinline__ int64_t token_of(const TileArgs& a, int blk, int r, bool& bad_frame) {
   bad_frame = false;
   if (a.flat) {
-    int64_t tok = (int64_t)blk * a.bs + r;
-    ok = tok < a.n_tokens;
-    return tok;
+    const int64_t tok = (int64_t)blk * a.bs + r;
+    return tok < a.n_tokens ? tok : -1;
   }
   const int cw = blk % a.nw;
   const int rem = blk / a.nw;
@@ -52,22 +51,23 @@ __device__ __forceinline__ int64_t token_of(const TileArgs& a, int blk, int r, b
   const int oh = rr % a.th;
   const int ot = rr / a.th;
   const int t = ct * a.tt + ot, h = ch * a.th + oh, w = cw * a.tw + ow;
-  ok = (t < a.T) && (h < a.LH) && (w < a.LW);
-  if (!ok) return 0;
+  if (t >= a.T || h >= a.LH || w >= a.LW) return -1;
   int64_t f = t;
   if (a.frame_ids) {
     f = a.frame_ids[t];
     if (f < 0 || f >= a.src_frames) {
-      ok = false;
       bad_frame = true;
-      return 0;
+      return -1;
     }
   }
   return (f * a.LH + h) * (int64_t)a.LW + w;
 }
 
+constexpr int kMaxBS = 1024;
+
 __global__ void tile_pool_kernel(const TileArgs a) {
   __shared__ double partial[8][kMaxD];
+  __shared__ int64_t rowtok[kMaxBS];  // raster token of each row of this block, -1 = zero row
   const int blk = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
@@ -79,13 +79,22 @@ __global__ void tile_pool_kernel(const TileArgs a) {
   const int epc = 16 / es;
   const bool pooling = (s == 0) && (a.pool != nullptr);
 
+  bool any_bad = false;
+  for (int r = threadIdx.x; r < a.bs; r += blockDim.x) {
+    bool bad;
+    rowtok[r] = token_of(a, blk, r, bad);
+    any_bad |= bad;
+  }
+  if (any_bad && a.err) atomicOr(a.err, (unsigned)LI_DEVERR_BAD_INDEX);
+  __syncthreads();
+
   const uint8_t* src = a.src[s] + (b * a.s_b[s] + h * a.s_h[s]) * es + c * 16;
+  const int64_t sl = a.s_l[s] * es;
   uint8_t* dst = a.dst[s] ? a.dst[s] + (b * a.d_b[s] + h * a.d_h[s] + (blk + a.dst_off) * a.d_n[s]) * es + c * 16
                           : nullptr;
   double acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.0;
-  bool any_bad = false;
 
   const int rows_per_thread = a.bs / 8;
   for (int i0 = 0; i0 < rows_per_thread; i0 += kUnroll) {
@@ -95,10 +104,8 @@ __global__ void tile_pool_kernel(const TileArgs a) {
       v[u] = make_uint4(0, 0, 0, 0);
       const int i = i0 + u;
       if (i < rows_per_thread) {
-        bool ok, bad;
-        const int64_t tok = token_of(a, blk, g + 8 * i, ok, bad);
-        any_bad |= bad;
-        if (ok) v[u] = __ldg(reinterpret_cast<const uint4*>(src + tok * a.s_l[s] * es));
+        const int64_t tok = rowtok[g + 8 * i];
+        if (tok >= 0) v[u] = __ldg(reinterpret_cast<const uint4*>(src + tok * sl));
       }
     }
 #pragma unroll
@@ -114,7 +121,6 @@ __global__ void tile_pool_kernel(const TileArgs a) {
       }
     }
   }
-  if (any_bad && a.err) atomicOr(a.err, (unsigned)LI_DEVERR_BAD_INDEX);
   if (a.pool == nullptr) return;
   if (pooling) {
 #pragma unroll

@@ -1,12 +1,14 @@
 // Block selection: pooled-score GEMM, protection bias, top-k, sorted emit.
 //
-// One CTA (8 warps) handles R query rows of one (b, h). Every thread takes key
-// rows j = tid, tid+256, ...: it (for 'cosine') normalises the key row, then
-// forms the R dot products with the query rows held in shared memory. Dot
-// products and squared norms are exact-product fp64 sums in d order, rounded
-// once to fp32 and then to the dtype; scalar multiplies/adds are single fp32
-// operations rounded to the dtype (torch's opmath rule). The ranking value is
-// mapped to torch's radix key and kept in shared memory.
+// One CTA (8 warps) handles R <= 8 query rows of one (b, h). The query rows
+// and then the key rows, 32 at a time, are staged in shared memory as floats
+// with coalesced 16-byte loads ('cosine' normalises them there). Warp r forms
+// the dot products of query row r with the 32 staged key rows, one per lane.
+// Dot products and squared norms are exact-product fp64 sums (four interleaved
+// partial sums over d, combined in order), rounded once to fp32 and then to
+// the dtype; scalar multiplies/adds are single fp32 operations rounded to the
+// dtype (torch's opmath rule). The ranking value is mapped to torch's radix
+// key and kept in shared memory.
 //
 // Warp r then selects row r's top k: a 64-bit composite key
 // (radix_key << idx_bits) | (2^idx_bits - 1 - j) is unique per column and
@@ -56,69 +58,96 @@ __device__ __forceinline__ uint32_t radix_key(float v, int dt) {
   return x ^ ((x & 0x8000u) ? 0xFFFFu : 0x8000u);
 }
 
-// Loads a pooled row as floats into `dst` (dtype values, exact), normalised
-// for 'cosine'. Executed by one thread per row.
-__device__ void load_row(const SelArgs& a, const uint8_t* row, float* dst) {
-  const int es = a.dtype == LI_DTYPE_FP32 ? 4 : 2;
-  double ss = 0.0;
-  for (int d = 0; d < a.D; ++d) {
-    const float x = load_dt(row, d, a.dtype);
-    dst[d] = x;
-    ss = fma((double)x, (double)x, ss);
+// Four interleaved fp64 partial sums of exact products, combined in order —
+// the summation order the CPU oracle restates.
+__device__ __forceinline__ double dot4(const float* x, const float* y, int D) {
+  double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
+  for (int d = 0; d < D; d += 4) {
+    p0 = fma((double)x[d], (double)y[d], p0);
+    p1 = fma((double)x[d + 1], (double)y[d + 1], p1);
+    p2 = fma((double)x[d + 2], (double)y[d + 2], p2);
+    p3 = fma((double)x[d + 3], (double)y[d + 3], p3);
   }
-  (void)es;
-  if (a.metric == LI_METRIC_COSINE) {
-    const float nrm = round_dt(__fsqrt_rn(__double2float_rn(ss)), a.dtype);
-    const float den = fmaxf(nrm, a.eps);
-    for (int d = 0; d < a.D; ++d) dst[d] = round_dt(__fdiv_rn(dst[d], den), a.dtype);
-  }
+  return ((p0 + p1) + p2) + p3;
 }
+
+// 16-byte chunk of a pooled row -> floats (exact widening).
+__device__ __forceinline__ void widen_chunk(const uint4& v, int dt, float* dst) {
+  const int epc = dt == LI_DTYPE_FP32 ? 4 : 8;
+  for (int e = 0; e < epc; ++e) dst[e] = chunk_elem(v, e, dt);
+}
+
+constexpr int kChunkRows = 32;
 
 template <int R>
 __global__ void __launch_bounds__(kThreads) select_kernel(const SelArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float* qs = reinterpret_cast<float*>(smem);                     // [R][D]
-  uint32_t* keys = reinterpret_cast<uint32_t*>(smem + sizeof(float) * R * a.D);  // [R][Nk]
+  const int pitch = a.D + 1;                                   // bank-conflict-free row pitch
+  float* qs = reinterpret_cast<float*>(smem);                   // [R][pitch]
+  float* ks = qs + R * pitch;                                   // [kChunkRows][pitch]
+  float* kden = ks + kChunkRows * pitch;                        // [kChunkRows]
+  float* qden = kden + kChunkRows;                              // [R]
+  uint32_t* keys = reinterpret_cast<uint32_t*>(qden + R);       // [R][Nk]
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
   const int q0 = blockIdx.x * R;
   const int nrows = min(R, a.Nq - q0);
   const int tid = threadIdx.x;
   const int es = a.dtype == LI_DTYPE_FP32 ? 4 : 2;
+  const int epc = 16 / es;
+  const int CH = a.D / epc;
+  const bool cosine = a.metric == LI_METRIC_COSINE;
 
-  if (tid < nrows)
-    load_row(a, a.qp + (b * a.q_b + h * a.q_h + (int64_t)(q0 + tid) * a.q_n) * es, qs + tid * a.D);
-  if (tid >= nrows && tid < R)
-    for (int d = 0; d < a.D; ++d) qs[tid * a.D + d] = 0.f;
+  // Query rows (normalised for 'cosine').
+  for (int i = tid; i < R * CH; i += kThreads) {
+    const int r = i / CH, c = i % CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nrows)
+      v = __ldg(reinterpret_cast<const uint4*>(a.qp + (b * a.q_b + h * a.q_h + (int64_t)(q0 + r) * a.q_n) * es) + c);
+    widen_chunk(v, a.dtype, qs + r * pitch + c * epc);
+  }
   __syncthreads();
+  if (cosine) {
+    if (tid < R) {
+      const float* x = qs + tid * pitch;
+      qden[tid] = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(dot4(x, x, a.D))), a.dtype), a.eps);
+    }
+    __syncthreads();
+    for (int i = tid; i < R * a.D; i += kThreads) {
+      const int r = i / a.D, d = i % a.D;
+      qs[r * pitch + d] = round_dt(__fdiv_rn(qs[r * pitch + d], qden[r]), a.dtype);
+    }
+  }
 
   const uint8_t* kbase = a.kp + (b * a.k_b + h * a.k_h) * es;
-  for (int j = tid; j < a.Nk; j += kThreads) {
-    const uint8_t* krow = kbase + (int64_t)j * a.k_n * es;
-    float den = 1.f;
-    if (a.metric == LI_METRIC_COSINE) {
-      double ss = 0.0;
-      for (int d = 0; d < a.D; ++d) {
-        const double x = (double)load_dt(krow, d, a.dtype);
-        ss = fma(x, x, ss);
+  const int warp = tid / 32, lane = tid % 32;
+  for (int c0 = 0; c0 < a.Nk; c0 += kChunkRows) {
+    __syncthreads();
+    for (int i = tid; i < kChunkRows * CH; i += kThreads) {
+      const int r = i / CH, c = i % CH;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (c0 + r < a.Nk) v = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)(c0 + r) * a.k_n * es) + c);
+      widen_chunk(v, a.dtype, ks + r * pitch + c * epc);
+    }
+    __syncthreads();
+    if (cosine) {
+      if (tid < kChunkRows) {
+        const float* x = ks + tid * pitch;
+        kden[tid] = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(dot4(x, x, a.D))), a.dtype), a.eps);
       }
-      den = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(ss)), a.dtype), a.eps);
+      __syncthreads();
+      for (int i = tid; i < kChunkRows * a.D; i += kThreads) {
+        const int r = i / a.D, d = i % a.D;
+        ks[r * pitch + d] = round_dt(__fdiv_rn(ks[r * pitch + d], kden[r]), a.dtype);
+      }
+      __syncthreads();
     }
-    double acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.0;
-    for (int d = 0; d < a.D; ++d) {
-      float x = load_dt(krow, d, a.dtype);
-      if (a.metric == LI_METRIC_COSINE) x = round_dt(__fdiv_rn(x, den), a.dtype);
-      const double xd = (double)x;
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[r] = fma((double)qs[r * a.D + d], xd, acc[r]);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (r >= nrows) break;
+    // Warp r forms the dot products of query row r with the 32 staged key rows.
+    for (int r = warp; r < nrows; r += kWarps) {
+      const int j = c0 + lane;
+      if (j >= a.Nk) continue;
       const int qi = q0 + r;
-      float s = round_dt(__double2float_rn(acc[r]), a.dtype);
+      float s = round_dt(__double2float_rn(dot4(qs + r * pitch, ks + lane * pitch, a.D)), a.dtype);
       if (a.metric == LI_METRIC_SCALED_DOT) s = round_dt(__fmul_rn(s, a.scale), a.dtype);
       if (a.bias)
         s = round_dt(__fadd_rn(s, a.bias[b * a.x_b + h * a.x_h + qi * a.x_q + (int64_t)j * a.x_k]), a.dtype);
@@ -138,7 +167,6 @@ __global__ void __launch_bounds__(kThreads) select_kernel(const SelArgs a) {
   }
   __syncthreads();
 
-  const int warp = tid / 32, lane = tid % 32;
   for (int r = warp; r < nrows; r += kWarps) {
     const int qi = q0 + r;
     const uint32_t* rk = keys + r * a.Nk;
@@ -255,7 +283,8 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
   if (!valid_dtype(dt) || k_pool->dtype != dt) return fail(LI_ERR_INVALID_ARG, "pool dtypes must match");
   if (k_pool->shape[0] != B || k_pool->shape[1] != H || k_pool->shape[3] != D)
     return fail(LI_ERR_SHAPE, "k_pool shape does not match q_pool");
-  if (q_pool->stride[3] != 1 || k_pool->stride[3] != 1) return fail(LI_ERR_STRIDE, "pools: D must be contiguous");
+  if (li_status st = check_vec_view(q_pool->data, q_pool->stride, 4, dt, D, "q_pool")) return st;
+  if (li_status st = check_vec_view(k_pool->data, k_pool->stride, 4, dt, D, "k_pool")) return st;
   if (D <= 0 || D > kMaxD) return fail(LI_ERR_UNSUPPORTED, "D=%lld", (long long)D);
   if (p->metric < LI_METRIC_COSINE || p->metric > LI_METRIC_DOT) return fail(LI_ERR_INVALID_ARG, "metric");
   int32_t ntxt, kb, nprot;
@@ -313,13 +342,16 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
                                 : __half2float(__float2half_rn(one_e6));
   }
   // Rows per CTA: as many (<= 8) as fit the shared-memory budget.
+  auto smem_of = [&](int r) {
+    return (size_t)4 * ((size_t)r * (D + 1) + (size_t)kChunkRows * (D + 1) + kChunkRows + r + (size_t)r * Nk);
+  };
   int R = 8;
-  while (R > 1 && (size_t)R * (D * 4 + Nk * 4) > kSmemBudget) R >>= 1;
-  if ((size_t)R * (D * 4 + Nk * 4) > kSmemBudget)
+  while (R > 1 && smem_of(R) > kSmemBudget) R >>= 1;
+  if (smem_of(R) > kSmemBudget)
     return fail(LI_ERR_UNSUPPORTED, "%lld key blocks exceed the selection kernel's shared memory", (long long)Nk);
   if (Nq < R) R = Nq >= 4 ? 4 : (Nq >= 2 ? 2 : 1);
   a.R = R;
-  const size_t smem = (size_t)R * (D * 4 + Nk * 4);
+  const size_t smem = smem_of(R);
   dim3 grid((unsigned)ceil_div(Nq, R), (unsigned)(B * H));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;

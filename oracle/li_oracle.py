@@ -21,8 +21,9 @@ the correctly rounded exact value:
   ``((p0+p1)+p2)+...+p7`` in fp64, rounded to fp32, divided by ``fp32(bs)`` in
   fp32, rounded to the dtype (RNE).
 * dot products in the block-score GEMM (``ar_sparse_operation.py:252-256``):
-  fp64 sum over d = 0..D-1 in order of exact products, rounded to fp32, then
-  to the dtype.
+  exact products summed in fp64 as four interleaved partial sums over d
+  (``p_g = sum_i x[4i+g]``, combined ``((p0+p1)+p2)+p3``), rounded to fp32,
+  then to the dtype.
 * ``F.normalize``: sum of squares as a dot product above, fp32 ``sqrt``,
   rounded to the dtype, clamped below at ``dtype(1e-12)``, then the
   element-wise fp32 quotient rounded to the dtype.
@@ -179,23 +180,38 @@ def tile_pool(x: np.ndarray, T: int, LH: int, LW: int, tile, dtype: str):
 # ----------------------------------------------------------------------------
 # Block selection
 # ----------------------------------------------------------------------------
+def _sum4(prod):
+    """Fixed-order fp64 sum over the last axis: four interleaved partial sums
+    ``p_g = sum_i x[4i+g]`` (sequential in i), combined ``((p0+p1)+p2)+p3``."""
+    D = prod.shape[-1]
+    parts = []
+    for g in range(4):
+        acc = np.zeros(prod.shape[:-1], np.float64)
+        for d in range(g, D, 4):
+            acc = acc + prod[..., d]
+        parts.append(acc)
+    return ((parts[0] + parts[1]) + parts[2]) + parts[3]
+
+
 def _dot_rows(a: np.ndarray, b: np.ndarray) -> np.ndarray:
-    """Sequential-in-d fp64 dot products ``a[..., i, :] . b[..., j, :]`` -> fp32."""
+    """fp64 dot products ``a[..., i, :] . b[..., j, :]`` of exact products in the
+    :func:`_sum4` order, rounded to fp32."""
     a64 = a.astype(np.float64)
     b64 = b.astype(np.float64)
     D = a.shape[-1]
-    acc = np.zeros(a.shape[:-1] + (b.shape[-2],), np.float64)
-    for d in range(D):
-        acc = acc + a64[..., :, None, d] * b64[..., None, :, d]
-    return acc.astype(np.float32)
+    parts = []
+    for g in range(4):
+        acc = np.zeros(a.shape[:-1] + (b.shape[-2],), np.float64)
+        for d in range(g, D, 4):
+            acc = acc + a64[..., :, None, d] * b64[..., None, :, d]
+        parts.append(acc)
+    return (((parts[0] + parts[1]) + parts[2]) + parts[3]).astype(np.float32)
 
 
 def normalize_rows(p: np.ndarray, dtype: str) -> np.ndarray:
     """``F.normalize(p, dim=-1)`` on a ``dtype`` tensor (``ar_sparse_operation.py:252``)."""
     p64 = p.astype(np.float64)
-    ss = np.zeros(p.shape[:-1], np.float64)
-    for d in range(p.shape[-1]):
-        ss = ss + p64[..., d] * p64[..., d]
+    ss = _sum4(p64 * p64)
     nrm = round_to(np.sqrt(ss.astype(np.float32)), dtype)
     eps = round_to(np.float32(1e-12), dtype)
     den = np.maximum(nrm, eps)
