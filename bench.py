@@ -255,6 +255,9 @@ def run_gpu(args, cfg, rank, world, local_rank):
     ms_e2e = s2.elapsed_time(e2)
     K.raise_device_errors(dev)
 
+    # The host-side reference sample runs on rank 0 before the last collective,
+    # so every rank leaves the process group together.
+    cpu = cpu_reference_sample(cfg) if rank == 0 else None
     t = torch.tensor([ms, ms_e2e, sum(attn_ms) / len(attn_ms)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -270,7 +273,7 @@ def run_gpu(args, cfg, rank, world, local_rank):
     traffic, tfile = _profile_traffic("attn_fwd_config5")
     if traffic is not None and world != 1:
         traffic = traffic // world
-    cpu_s, cpu_fl, threads = cpu_reference_sample(cfg)
+    cpu_s, cpu_fl, threads = cpu
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "ms_per_call": attn_call_ms,

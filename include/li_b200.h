@@ -171,6 +171,16 @@ li_status li_rank_blocks(const li_view4* rank_scores, int32_t score_dtype, int32
                          int32_t text_len, int32_t bs, li_index_view* out, void* stream);
 
 /* ---- (a6, a7, a8) block-sparse attention forward ----------------------- */
+/* Split-KV workspace. When a launch has too few query blocks to fill the GPU,
+ * each block's list is split over several CTAs that write fp32 partials
+ * (O, row max, row sum) to a caller-provided device workspace, merged by a
+ * second kernel. This returns the bytes the attention entry points will use
+ * for that shape (0 = no split). A smaller or NULL workspace is allowed and
+ * simply disables the split. No reference counterpart (the reference always
+ * launches one program per 128 query rows). */
+li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks,
+                                         int64_t max_blocks_per_row, int32_t head_dim, int64_t* bytes);
+
 /* Tiled form — replaces longcat_flash_attn / _attn_fwd_bsa_align
  * (hy-worldplay/.../longcat_kernel.py:27-233; matrix-game-3.0/.../longcat_kernel.py:28-190).
  * q [B,H,Q_len,D], k/v [B,H,K_len,D] in the tiled order, K_len % bs == 0.
@@ -180,7 +190,8 @@ li_status li_rank_blocks(const li_view4* rank_scores, int32_t score_dtype, int32
  * D in {64, 128}; bs in {64, 128}; q/k/v/o bf16 or fp16 (all the same). */
 li_status li_sparse_attn_tiled(const li_view4* q, const li_view4* k, const li_view4* v,
                                const li_index_view* idx, int32_t bs, float sm_scale,
-                               li_view4* o, float* lse, uint32_t* err_word, void* stream);
+                               li_view4* o, float* lse, uint32_t* err_word,
+                               void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Raster form (fused tile -> attention -> untile): reads q and the visual K/V
  * straight from their raster layouts in 3D blocks (zero-filled past the grid
@@ -192,7 +203,8 @@ li_status li_sparse_attn_raster(const li_view4* q, li_grid3d grid_q,
                                 const li_view4* k_txt, const li_view4* v_txt,
                                 const li_view4* k_vis, const li_view4* v_vis, li_grid3d grid_k,
                                 const li_index_view* idx, float sm_scale,
-                                li_view4* o, float* lse, uint32_t* err_word, void* stream);
+                                li_view4* o, float* lse, uint32_t* err_word,
+                                void* workspace, int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

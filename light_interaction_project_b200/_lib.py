@@ -78,11 +78,12 @@ SIGNATURES = {
     "li_select_blocks": ([POINTER(View4), POINTER(View4), POINTER(SelectParams), POINTER(View4), POINTER(IndexView),
                           POINTER(View4), c_void_p], c_int32),
     "li_rank_blocks": ([POINTER(View4), c_int32, c_int32, c_int32, c_int32, POINTER(IndexView), c_void_p], c_int32),
+    "li_sparse_attn_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, c_int32, POINTER(c_int64)], c_int32),
     "li_sparse_attn_tiled": ([POINTER(View4), POINTER(View4), POINTER(View4), POINTER(IndexView), c_int32, c_float,
-                              POINTER(View4), c_void_p, c_void_p, c_void_p], c_int32),
+                              POINTER(View4), c_void_p, c_void_p, c_void_p, c_int64, c_void_p], c_int32),
     "li_sparse_attn_raster": ([POINTER(View4), Grid3d, POINTER(View4), POINTER(View4), POINTER(View4),
                                POINTER(View4), Grid3d, POINTER(IndexView), c_float, POINTER(View4), c_void_p,
-                               c_void_p, c_void_p], c_int32),
+                               c_void_p, c_void_p, c_int64, c_void_p], c_int32),
 }
 
 

@@ -69,6 +69,13 @@ struct __align__(64) Params {
   int32_t k_nh, k_nw, k_tt, k_th, k_tw;
   int32_t ntxt, n_kv, nq;
   int32_t smax;  // index-row width: counts are clamped to it
+  // Split-KV: CTA (qi, sp) handles list entries [S*sp/nsplit, S*(sp+1)/nsplit) and,
+  // when nsplit > 1, writes its unnormalised fp32 partial (O, m, l) to `part`
+  // (unit u = ((b*H + h)*nq + qi)*nsplit + sp: O at part + u*128*D, m and l
+  // after all O blocks) for attn_combine_kernel.
+  int32_t nsplit;
+  float* part;
+  int64_t part_units;
 };
 
 // ------------------------------- PTX helpers -------------------------------
@@ -266,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qi = blockIdx.x;
+  const int qi = blockIdx.x / p.nsplit, sp = blockIdx.x % p.nsplit;
   const int bl = blockIdx.y / p.H, h = blockIdx.y % p.H;
   const int b = p.b0 + bl;
   const int mi = p.per_batch ? bl : 0;
@@ -288,9 +295,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   float* xl = xm + 2 * 128;                                 // [2 chains][128] row sum
 
   const int S_raw = p.cnt[b * p.c_b + h * p.c_h + (int64_t)qi * p.c_q];
-  const int S = S_raw < 0 ? 0 : (S_raw > p.smax ? p.smax : S_raw);
-  if (S != S_raw && threadIdx.x == 0 && p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
-  const int32_t* irow = p.idx + b * p.i_b + h * p.i_h + (int64_t)qi * p.i_q;
+  const int S_all = S_raw < 0 ? 0 : (S_raw > p.smax ? p.smax : S_raw);
+  if (S_all != S_raw && threadIdx.x == 0 && sp == 0 && p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
+  const int j_lo = (int)(((int64_t)S_all * sp) / p.nsplit), j_hi = (int)(((int64_t)S_all * (sp + 1)) / p.nsplit);
+  const int S = j_hi - j_lo;  // this CTA's share of the list
+  const int32_t* irow = p.idx + b * p.i_b + h * p.i_h + (int64_t)qi * p.i_q + (int64_t)j_lo * p.i_s;
+  const bool partial = p.nsplit > 1;
   const int n_chain[2] = {(S + 1) / 2, S / 2};  // blocks of chain 0 (even j) and chain 1 (odd j)
 
   if (threadIdx.x == 0) {
@@ -516,7 +526,39 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const float lt = a0 * l0 + a1 * l1;
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
     const bool store = ok && !*abort_flag;
-    if (store) {
+    if (partial) {
+      // Unnormalised partial of this split: O = a0 O_0 + a1 O_1 relative to mm.
+      const int64_t unit = ((int64_t)(b * p.H + h) * p.nq + qi) * p.nsplit + sp;
+      float* po = p.part + unit * 128 * D + (int64_t)row * D;
+      constexpr int kOCols = D / 2;
+      const uint32_t o0 = tmem + lane_base + kColO, o1 = tmem + lane_base + kColO + 128;
+      if (store) {
+#pragma unroll
+        for (int cc = 0; cc < kOCols / 32; ++cc) {
+          const int col0 = w * kOCols + cc * 32;
+          uint32_t x0[32], x1[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) { x0[e] = 0u; x1[e] = 0u; }
+          if (l0 > 0.f) tmem_ld32(o0 + col0, x0);
+          if (l1 > 0.f) tmem_ld32(o1 + col0, x1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 v;
+            v.x = (l0 > 0.f ? __uint_as_float(x0[e]) * a0 : 0.f) + (l1 > 0.f ? __uint_as_float(x1[e]) * a1 : 0.f);
+            v.y = (l0 > 0.f ? __uint_as_float(x0[e + 1]) * a0 : 0.f) + (l1 > 0.f ? __uint_as_float(x1[e + 1]) * a1 : 0.f);
+            v.z = (l0 > 0.f ? __uint_as_float(x0[e + 2]) * a0 : 0.f) + (l1 > 0.f ? __uint_as_float(x1[e + 2]) * a1 : 0.f);
+            v.w = (l0 > 0.f ? __uint_as_float(x0[e + 3]) * a0 : 0.f) + (l1 > 0.f ? __uint_as_float(x1[e + 3]) * a1 : 0.f);
+            *reinterpret_cast<float4*>(po + col0 + e) = v;
+          }
+        }
+        if (w == 0) {
+          float* pml = p.part + p.part_units * 128 * D;
+          pml[unit * 128 + row] = lt > 0.f ? mm : -INFINITY;
+          pml[p.part_units * 128 + unit * 128 + row] = lt;
+        }
+      }
+    } else if (store) {
       uint8_t* stage = smem + L::kOffQ;
       constexpr int kOCols = D / 2;  // this warpgroup converts O columns [w*D/2, (w+1)*D/2)
       const uint32_t o0 = tmem + lane_base + kColO, o1 = tmem + lane_base + kColO + 128;
@@ -551,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(bar_st);
-    if (store && threadIdx.x == 0 && mbar_wait(bar_st, 0, abort_flag, p.err) && !*abort_flag) {
+    if (store && !partial && threadIdx.x == 0 && mbar_wait(bar_st, 0, abort_flag, p.err) && !*abort_flag) {
       int c[5];
       block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
       for (int hf = 0; hf < L::kHalves; ++hf) {
@@ -560,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
       tma_store_commit_and_drain();
     }
-    if (store && w == 0 && p.lse && row < BS)
+    if (store && !partial && w == 0 && p.lse && row < BS)
       p.lse[(int64_t)(b * p.H + h) * p.lse_len + (int64_t)qi * BS + row] = lt > 0.f ? mm + __log2f(lt) : -INFINITY;
   }
   tc_fence_before();
@@ -568,6 +610,76 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (warp == kWarpMMA0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+
+// ------------------------- split-KV combine kernel -------------------------
+// One CTA per (query block, b*h), one thread per tile row: merges the nsplit
+// partials O_s (unnormalised, reference max m_s, row sum l_s):
+//   M = max m_s,  w_s = 2^(m_s - M),  O = sum w_s O_s / sum w_s l_s,
+// and stores the row at its raster (or tiled) position in o.
+struct CombineArgs {
+  const float* part;
+  int64_t part_units;
+  uint8_t* o;
+  int64_t o_b, o_h, o_l;
+  float* lse;
+  int64_t lse_len;
+  int32_t H, nq, nsplit, D, bs, f16;
+  int32_t q_raster, T, LH, LW, tt, th, tw, nh, nw;
+  int64_t q_len;  // tiled form: valid query rows
+};
+
+__global__ void __launch_bounds__(128) attn_combine_kernel(const CombineArgs a) {
+  const int qi = blockIdx.x, bh = blockIdx.y, row = threadIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  if (row >= a.bs) return;
+  int64_t tok;
+  if (a.q_raster) {
+    const int cw = qi % a.nw, rem = qi / a.nw, ch = rem % a.nh, ct = rem / a.nh;
+    const int ow = row % a.tw, rr = row / a.tw, oh = rr % a.th, ot = rr / a.th;
+    const int t = ct * a.tt + ot, hh = ch * a.th + oh, w = cw * a.tw + ow;
+    tok = (t < a.T && hh < a.LH && w < a.LW) ? ((int64_t)t * a.LH + hh) * a.LW + w : -1;
+  } else {
+    tok = (int64_t)qi * a.bs + row;
+    if (tok >= a.q_len) tok = -1;
+  }
+  const int64_t unit0 = ((int64_t)bh * a.nq + qi) * a.nsplit;
+  const float* pm = a.part + a.part_units * 128 * a.D;
+  const float* pl = pm + a.part_units * 128;
+  float M = -INFINITY;
+  for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, pm[(unit0 + sp) * 128 + row]);
+  float L = 0.f;
+  for (int sp = 0; sp < a.nsplit; ++sp) {
+    const float l = pl[(unit0 + sp) * 128 + row];
+    if (l > 0.f) L += ex2(pm[(unit0 + sp) * 128 + row] - M) * l;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if (a.lse && tok >= 0 && row < a.bs)
+    a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + row] = L > 0.f ? M + __log2f(L) : -INFINITY;
+  if (tok < 0) return;
+  uint8_t* dst = a.o + (b * a.o_b + h * a.o_h + tok * a.o_l) * 2;
+  for (int d0 = 0; d0 < a.D; d0 += 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < a.nsplit; ++sp) {
+      const float l = pl[(unit0 + sp) * 128 + row];
+      if (!(l > 0.f)) continue;
+      const float wgt = ex2(pm[(unit0 + sp) * 128 + row] - M) * inv;
+      const float4* src = reinterpret_cast<const float4*>(a.part + ((unit0 + sp) * 128 + row) * a.D + d0);
+      const float4 x = src[0], y = src[1];
+      acc[0] += wgt * x.x; acc[1] += wgt * x.y; acc[2] += wgt * x.z; acc[3] += wgt * x.w;
+      acc[4] += wgt * y.x; acc[5] += wgt * y.y; acc[6] += wgt * y.z; acc[7] += wgt * y.w;
+    }
+    uint4 v;
+    if (a.f16) {
+      v.x = pack2<true>(acc[0], acc[1]); v.y = pack2<true>(acc[2], acc[3]);
+      v.z = pack2<true>(acc[4], acc[5]); v.w = pack2<true>(acc[6], acc[7]);
+    } else {
+      v.x = pack2<false>(acc[0], acc[1]); v.y = pack2<false>(acc[2], acc[3]);
+      v.z = pack2<false>(acc[4], acc[5]); v.w = pack2<false>(acc[6], acc[7]);
+    }
+    *reinterpret_cast<uint4*>(dst + d0 * 2) = v;
   }
 }
 
@@ -662,6 +774,33 @@ MapSpec rows_spec(const li_view4& v, int bs, const BHPlan& pl, int b, int es) {
 
 using KernelFn = void (*)(Params);
 
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// Number of list splits per query block. With one CTA per SM, a launch of
+// `tiles` CTAs keeps tiles / (waves * SMs) of the machine busy; when that is
+// under 85%, split each list into the fewest parts that reach 90% (a split
+// costs a second prologue per CTA and the combine pass).
+int split_plan(int64_t tiles, int64_t smax) {
+  const int64_t sms = sm_count();
+  auto eff = [&](int64_t units) { return (double)units / (double)(((units + sms - 1) / sms) * sms); };
+  if (tiles <= 0 || eff(tiles) >= 0.85) return 1;
+  int best = 1;
+  double best_eff = eff(tiles);
+  for (int ns = 2; ns <= 8; ++ns) {
+    if (smax / ns < 8) break;
+    const double e = eff(tiles * ns);
+    if (e > best_eff) { best = ns; best_eff = e; }
+    if (e >= 0.90) break;
+  }
+  return best;
+}
+
+int64_t workspace_bytes(int64_t units, int64_t D) { return units * 128 * (D + 2) * 4; }
+
 template <int D, int BS, bool F16>
 li_status launch_t(const Params& prm, dim3 grid, cudaStream_t stream) {
   using L = Smem<D, BS>;
@@ -697,7 +836,8 @@ li_status check_operand(const li_view4* v, const char* name, int dtype, int64_t 
 // Shared driver of both public forms.
 li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_view4* k, const li_view4* v,
               bool kv_raster, const li_grid3d* gk, const li_view4* kt, const li_view4* vt, int bs,
-              const li_index_view* idx, float sm_scale, li_view4* o, float* lse, uint32_t* err, void* stream) {
+              const li_index_view* idx, float sm_scale, li_view4* o, float* lse, uint32_t* err, void* workspace,
+              int64_t workspace_bytes_avail, void* stream) {
   if (!q || !q->data) return fail(LI_ERR_INVALID_ARG, "q is required");
   const int dtype = q->dtype;
   if (dtype != LI_DTYPE_BF16 && dtype != LI_DTYPE_FP16)
@@ -760,6 +900,16 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
   prm.ntxt = ntxt; prm.n_kv = (int)n_kv; prm.nq = (int)nq;
   if (idx->shape[3] < 0 || idx->shape[3] > (1ll << 30)) return fail(LI_ERR_SHAPE, "bad index-row width");
   prm.smax = (int)idx->shape[3];
+  prm.nsplit = 1;
+  {
+    const int ns = split_plan(B * H * nq, idx->shape[3]);
+    const int64_t units = B * H * nq * ns;
+    if (ns > 1 && workspace && workspace_bytes_avail >= workspace_bytes(units, D) && aligned16(workspace)) {
+      prm.nsplit = ns;
+      prm.part = static_cast<float*>(workspace);
+      prm.part_units = units;
+    }
+  }
   if (nq == 0 || B * H == 0) return LI_OK;
 
   // All operands share one (b, h) addressing plan; fall back to per-batch
@@ -800,9 +950,25 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
       }
       if (st) return st;
     }
-    dim3 grid((unsigned)nq, (unsigned)(nb * H));
+    dim3 grid((unsigned)(nq * prm.nsplit), (unsigned)(nb * H));
     if (nb * H > 65535) return fail(LI_ERR_SHAPE, "B*H too large for one launch");
     if (li_status st = launch((int)D, bs, f16, prm, grid, static_cast<cudaStream_t>(stream))) return st;
+  }
+  if (prm.nsplit > 1) {
+    CombineArgs ca;
+    memset(&ca, 0, sizeof(ca));
+    ca.part = prm.part; ca.part_units = prm.part_units;
+    ca.o = static_cast<uint8_t*>(o->data); ca.o_b = o->stride[0]; ca.o_h = o->stride[1]; ca.o_l = o->stride[2];
+    ca.lse = lse; ca.lse_len = nq * bs;
+    ca.H = (int)H; ca.nq = (int)nq; ca.nsplit = prm.nsplit; ca.D = (int)D; ca.bs = bs; ca.f16 = f16;
+    ca.q_raster = q_raster;
+    if (q_raster) {
+      ca.T = gq->T; ca.LH = gq->LH; ca.LW = gq->LW; ca.tt = gq->tt; ca.th = gq->th; ca.tw = gq->tw;
+      ca.nh = prm.q_nh; ca.nw = prm.q_nw;
+    }
+    ca.q_len = q->shape[2];
+    attn_combine_kernel<<<dim3((unsigned)nq, (unsigned)(B * H)), 128, 0, static_cast<cudaStream_t>(stream)>>>(ca);
+    if (li_status st = cuda_status(cudaGetLastError(), "attention combine launch")) return st;
   }
   return LI_OK;
 }
@@ -812,21 +978,31 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
 
 using namespace li;
 
+extern "C" li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks,
+                                                    int64_t max_blocks_per_row, int32_t head_dim, int64_t* bytes) {
+  if (!bytes) return fail(LI_ERR_INVALID_ARG, "bytes is required");
+  const int ns = attn::split_plan(batch * heads * n_q_blocks, max_blocks_per_row);
+  *bytes = ns > 1 ? attn::workspace_bytes(batch * heads * n_q_blocks * ns, head_dim) : 0;
+  return LI_OK;
+}
+
 extern "C" li_status li_sparse_attn_tiled(const li_view4* q, const li_view4* k, const li_view4* v,
                                           const li_index_view* idx, int32_t bs, float sm_scale, li_view4* o,
-                                          float* lse, uint32_t* err_word, void* stream) {
+                                          float* lse, uint32_t* err_word, void* workspace, int64_t workspace_bytes,
+                                          void* stream) {
   return attn::run(q, false, nullptr, k, v, false, nullptr, nullptr, nullptr, bs, idx, sm_scale, o, lse, err_word,
-                   stream);
+                   workspace, workspace_bytes, stream);
 }
 
 extern "C" li_status li_sparse_attn_raster(const li_view4* q, li_grid3d grid_q, const li_view4* k_txt,
                                            const li_view4* v_txt, const li_view4* k_vis, const li_view4* v_vis,
                                            li_grid3d grid_k, const li_index_view* idx, float sm_scale, li_view4* o,
-                                           float* lse, uint32_t* err_word, void* stream) {
+                                           float* lse, uint32_t* err_word, void* workspace, int64_t workspace_bytes,
+                                           void* stream) {
   if (grid_q.tt != grid_k.tt || grid_q.th != grid_k.th || grid_q.tw != grid_k.tw || grid_q.LH != grid_k.LH ||
       grid_q.LW != grid_k.LW)
     return fail(LI_ERR_SHAPE, "grid_q and grid_k must share the latent size and tile");
   const int bs = grid_q.tt * grid_q.th * grid_q.tw;
   return attn::run(q, true, &grid_q, k_vis, v_vis, true, &grid_k, k_txt, v_txt, bs, idx, sm_scale, o, lse, err_word,
-                   stream);
+                   workspace, workspace_bytes, stream);
 }

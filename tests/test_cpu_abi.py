@@ -73,14 +73,25 @@ def test_entry_points_validate_before_launch(lib):
     v.dtype = L.DTYPE_FP32
     iv = L.IndexView()
     st = lib.li_sparse_attn_tiled(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(iv), 128, 1.0,
-                                  ctypes.byref(v), None, None, None)
+                                  ctypes.byref(v), None, None, None, 0, None)
     assert st == L.LI_ERR_UNSUPPORTED
     v.dtype = L.DTYPE_BF16
     st = lib.li_sparse_attn_tiled(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(iv), 96, 1.0,
-                                  ctypes.byref(v), None, None, None)
+                                  ctypes.byref(v), None, None, None, 0, None)
     assert st == L.LI_ERR_UNSUPPORTED
     with pytest.raises(NotImplementedError):
         L.check(st, "attn")
+
+
+def test_split_plan_workspace(lib):
+    """Split-KV engages only when a launch leaves most of the last wave idle."""
+    nbytes = ctypes.c_int64()
+    assert lib.li_sparse_attn_workspace_bytes(1, 24, 56, 238, 128, ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 0                     # 1344 query blocks: ~9 full waves on 148 SMs
+    assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 238, 128, ctypes.byref(nbytes)) == 0
+    assert nbytes.value > 0 and nbytes.value % (128 * 130 * 4) == 0   # 168 query blocks: split
+    assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 8, 128, ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 0                     # too few blocks per row to split
 
 
 def test_rank_blocks_rejects_k_out_of_range(lib):

@@ -213,3 +213,46 @@ def test_reference_fixtures_end_to_end(cuda_ok, name):
             ref_rows = g["out_ref"][b, h, rows]
         if rows.size:
             assert_close_bf16(got[b, h, rows], ref_rows, what=f"{name} b{b} h{h}")
+
+
+@pytest.mark.parametrize("D,bs", [(128, 128), (64, 64)])
+def test_split_kv_partials_merge(cuda_ok, D, bs):
+    """Few query blocks -> the list of each is split over CTAs writing fp32
+    partials (some splits empty) that the combine kernel merges."""
+    from light_interaction_project_b200 import _lib as LL
+    import ctypes
+    B, H, nq, nkb, S = 1, 2, 5, 60, 40
+    nb = ctypes.c_int64()
+    LL.load().li_sparse_attn_workspace_bytes(B, H, nq, S, D, ctypes.byref(nb))
+    assert nb.value > 0, "this shape must take the split path"
+    q, tq = rand((B, H, nq * bs, D), 901, "bf16")
+    k, tk = rand((B, H, nkb * bs, D), 902, "bf16")
+    v, tv = rand((B, H, nkb * bs, D), 903, "bf16")
+    idx, cnt = _random_lists(np.random.default_rng(3), B, H, nq, nkb, S)
+    cnt[0, 0, 1] = 2   # fewer blocks than splits
+    cnt[0, 1, 2] = 0   # empty list
+    out, lse = K.sparse_attn_tiled(tq, tk, tv, torch.from_numpy(idx).to(dev()), torch.from_numpy(cnt).to(dev()),
+                                   bs, return_lse=True)
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    ref, ref_lse = O.sparse_attention_tiled(q.reshape(B, H, nq, bs, D), k.reshape(B, H, nkb, bs, D),
+                                            v.reshape(B, H, nkb, bs, D), idx, cnt, p_dtype="bf16")
+    assert_close_bf16(to_np(out), ref.reshape(B, H, nq * bs, D))
+    got_lse = to_np(lse)
+    fin = np.isfinite(ref_lse.reshape(B, H, -1))
+    np.testing.assert_allclose(got_lse[fin], ref_lse.reshape(B, H, -1)[fin], atol=2e-3, rtol=1e-4)
+    assert np.isneginf(got_lse[~fin]).all()
+
+
+def test_split_kv_raster_few_heads(cuda_ok):
+    """The head-sharded shape at 8 GPUs (3 heads, 56 query blocks) through the MG path."""
+    B, H, D, LH, LW, F = 1, 3, 128, 30, 52, 8
+    q, tq = rand((B, H, 4 * LH * LW, D), 911, "bf16")
+    k, tk = rand((B, H, F * LH * LW, D), 912, "bf16")
+    v, tv = rand((B, H, F * LH * LW, D), 913, "bf16")
+    params = dict(tile_size=(4, 4, 8), topk_ratio=0.5, sim_metric="cosine")
+    nq, nk = 56, 112
+    out = mg.run_sparse_attention(tq, tk, tv, 0, 0, (LH, LW), params, q_block_offset=nk - nq)
+    torch.cuda.synchronize()
+    ref, _ = O.run_sparse_attention_mg(q, k, v, 0, (LH, LW), params, "bf16", q_offset=nk - nq)
+    assert_close_bf16(to_np(out), ref)
