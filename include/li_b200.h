@@ -158,10 +158,25 @@ li_status li_select_budget(const li_select_params* p, int64_t n_q_blocks, int64_
  * Writes indices [B,H,Nq,ntxt+budget] (int32, ascending, text blocks first) and
  * counts [B,H,Nq]. `score_bias` (optional fp32 [B,H,Nq,Nk] view, harness
  * extension) is added to the similarity before the protection bias.
- * `rank_out` (optional fp32 [B,H,Nq,Nk]) receives the ranking scores. */
+ * `rank_out` (optional fp32 [B,H,Nq,Nk]) receives the ranking scores.
+ * `workspace` (optional, li_select_workspace_bytes() bytes, 16-byte aligned)
+ * lets the scores and the top-k run as two wide kernels; without it one
+ * kernel does both (same results, bit for bit). */
 li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_pool,
                            const li_select_params* p, const li_view4* score_bias,
-                           li_index_view* out, li_view4* rank_out, void* stream);
+                           li_index_view* out, li_view4* rank_out,
+                           void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Bytes of the optional selection workspace (0 when the shape cannot use it). */
+li_status li_select_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks, int64_t n_k_blocks,
+                                    int64_t* bytes);
+
+/* Row-wise F.normalize (dim=-1) of pooled rows, with the selection kernel's
+ * exact rounding chain: y = dtype(x / max(dtype(sqrt(fp32(sum x^2))), dtype(1e-12))).
+ * Cosine selection equals the plain-dot selection of normalised pools, so the
+ * pipeline normalises each pool once here instead of in every selection CTA —
+ * the F.normalize calls of ar_sparse_operation.py:252 / bi_sparse_operation.py:197. */
+li_status li_normalize_rows(const li_view4* x, li_view4* y, void* stream);
 
 /* The ranking step alone on given ranking scores (fp32 [B,H,Nq,Nk] holding
  * `dtype` values): top-`k` by the dtype's radix order, ties to the lowest

@@ -76,7 +76,9 @@ SIGNATURES = {
     "li_gather_frames": ([POINTER(View4), c_void_p, c_int32, c_int32, POINTER(View4), c_void_p, c_void_p], c_int32),
     "li_select_budget": ([POINTER(SelectParams), c_int64, c_int64, POINTER(c_int32), POINTER(c_int32)], c_int32),
     "li_select_blocks": ([POINTER(View4), POINTER(View4), POINTER(SelectParams), POINTER(View4), POINTER(IndexView),
-                          POINTER(View4), c_void_p], c_int32),
+                          POINTER(View4), c_void_p, c_int64, c_void_p], c_int32),
+    "li_select_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, POINTER(c_int64)], c_int32),
+    "li_normalize_rows": ([POINTER(View4), POINTER(View4), c_void_p], c_int32),
     "li_rank_blocks": ([POINTER(View4), c_int32, c_int32, c_int32, c_int32, POINTER(IndexView), c_void_p], c_int32),
     "li_sparse_attn_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, c_int32, POINTER(c_int64)], c_int32),
     "li_sparse_attn_tiled": ([POINTER(View4), POINTER(View4), POINTER(View4), POINTER(IndexView), c_int32, c_float,

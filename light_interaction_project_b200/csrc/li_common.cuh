@@ -44,6 +44,43 @@ __device__ __forceinline__ float chunk_elem(const uint4& v, int i, int dt) {
   return __half2float(__ushort_as_half(h));
 }
 
+// Exact widening of a 16-bit float (bf16 / fp16 bits) or an fp32 to double,
+// built from the bit fields with integer operations (no float-to-double
+// conversion instruction). Zero, subnormal, infinite and NaN inputs take the
+// conversion path.
+__device__ __forceinline__ double bf16_bits_to_f64(uint32_t b) {
+  const uint32_t e = (b >> 7) & 0xFFu;
+  if (e - 1u < 0xFEu)
+    return __longlong_as_double((long long)(((uint64_t)(b >> 15) << 63) | ((uint64_t)(e + 896u) << 52) |
+                                            ((uint64_t)(b & 0x7Fu) << 45)));
+  if ((b & 0x7FFFu) == 0u) return __longlong_as_double((long long)((uint64_t)(b >> 15) << 63));
+  return (double)__uint_as_float(b << 16);
+}
+__device__ __forceinline__ double fp16_bits_to_f64(uint32_t h) {
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  if (e - 1u < 0x1Eu)
+    return __longlong_as_double((long long)(((uint64_t)(h >> 15) << 63) | ((uint64_t)(e + 1008u) << 52) |
+                                            ((uint64_t)(h & 0x3FFu) << 42)));
+  if ((h & 0x7FFFu) == 0u) return __longlong_as_double((long long)((uint64_t)(h >> 15) << 63));
+  return (double)__half2float(__ushort_as_half((unsigned short)h));
+}
+__device__ __forceinline__ double fp32_bits_to_f64(uint32_t f) {
+  const uint32_t e = (f >> 23) & 0xFFu;
+  if (e - 1u < 0xFEu)
+    return __longlong_as_double((long long)(((uint64_t)(f >> 31) << 63) | ((uint64_t)(e + 896u) << 52) |
+                                            ((uint64_t)(f & 0x7FFFFFu) << 29)));
+  if ((f & 0x7FFFFFFFu) == 0u) return __longlong_as_double((long long)((uint64_t)(f >> 31) << 63));
+  return (double)__uint_as_float(f);
+}
+// Element `i` of a 16-byte chunk as double (exact).
+__device__ __forceinline__ double chunk_elem_f64(const uint4& v, int i, int dt) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if (dt == LI_DTYPE_FP32) return fp32_bits_to_f64(w[i]);
+  const uint32_t word = w[i >> 1];
+  const uint32_t h = (i & 1) ? (word >> 16) : (word & 0xFFFFu);
+  return dt == LI_DTYPE_BF16 ? bf16_bits_to_f64(h) : fp16_bits_to_f64(h);
+}
+
 // Store a dtype-representable float as the dtype at p.
 __device__ __forceinline__ void store_dt(void* p, int64_t i, float x, int dt) {
   if (dt == LI_DTYPE_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x);

@@ -15,7 +15,8 @@ namespace li {
 namespace {
 
 constexpr int kMaxD = 256;
-constexpr int kUnroll = 8;
+constexpr int kUnroll = 8;       // 16-byte copies in flight per thread (gather)
+constexpr int kPoolUnroll = 8;   // rows in flight per thread (pool / tile)
 
 struct TileArgs {
   const uint8_t* src[2];
@@ -65,9 +66,10 @@ __device__ __forceinline__ int64_t token_of(const TileArgs& a, int blk, int r, b
 
 constexpr int kMaxBS = 1024;
 
-__global__ void tile_pool_kernel(const TileArgs a) {
-  __shared__ double partial[8][kMaxD];
-  __shared__ int64_t rowtok[kMaxBS];  // raster token of each row of this block, -1 = zero row
+__global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  double* partial = reinterpret_cast<double*>(smem);                // [8][D]
+  int32_t* rowtok = reinterpret_cast<int32_t*>(partial + 8 * a.D);  // token of each row, -1 = zero row
   const int blk = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
@@ -82,7 +84,7 @@ __global__ void tile_pool_kernel(const TileArgs a) {
   bool any_bad = false;
   for (int r = threadIdx.x; r < a.bs; r += blockDim.x) {
     bool bad;
-    rowtok[r] = token_of(a, blk, r, bad);
+    rowtok[r] = (int32_t)token_of(a, blk, r, bad);
     any_bad |= bad;
   }
   if (any_bad && a.err) atomicOr(a.err, (unsigned)LI_DEVERR_BAD_INDEX);
@@ -97,19 +99,19 @@ __global__ void tile_pool_kernel(const TileArgs a) {
   for (int e = 0; e < 8; ++e) acc[e] = 0.0;
 
   const int rows_per_thread = a.bs / 8;
-  for (int i0 = 0; i0 < rows_per_thread; i0 += kUnroll) {
-    uint4 v[kUnroll];
+  for (int i0 = 0; i0 < rows_per_thread; i0 += kPoolUnroll) {
+    uint4 v[kPoolUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kPoolUnroll; ++u) {
       v[u] = make_uint4(0, 0, 0, 0);
       const int i = i0 + u;
       if (i < rows_per_thread) {
-        const int64_t tok = rowtok[g + 8 * i];
-        if (tok >= 0) v[u] = __ldg(reinterpret_cast<const uint4*>(src + tok * sl));
+        const int32_t tok = rowtok[g + 8 * i];
+        if (tok >= 0) v[u] = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)tok * sl));
       }
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kPoolUnroll; ++u) {
       const int i = i0 + u;
       if (i < rows_per_thread) {
         if (dst) *reinterpret_cast<uint4*>(dst + (int64_t)(g + 8 * i) * a.d_r[s] * es) = v[u];
@@ -125,16 +127,16 @@ __global__ void tile_pool_kernel(const TileArgs a) {
   if (pooling) {
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-      if (e < epc) partial[g][c * epc + e] = acc[e];
+      if (e < epc) partial[g * a.D + c * epc + e] = acc[e];
   }
   __syncthreads();
   if (pooling && g == 0) {
     uint8_t* pp = a.pool + (b * a.p_b + h * a.p_h + (blk + a.pool_off) * a.p_n) * es;
     for (int e = 0; e < epc; ++e) {
       const int col = c * epc + e;
-      double tot = partial[0][col];
+      double tot = partial[col];
 #pragma unroll
-      for (int gg = 1; gg < 8; ++gg) tot = tot + partial[gg][col];
+      for (int gg = 1; gg < 8; ++gg) tot = tot + partial[gg * a.D + col];
       const float mean = __fdiv_rn(__double2float_rn(tot), (float)a.bs);
       store_dt(pp, col, round_dt(mean, a.dtype), a.dtype);
     }
@@ -240,7 +242,8 @@ li_status launch_tile(TileArgs& a, int64_t nblk, int64_t B, int64_t H, void* str
   if (nblk > 2147483647 || B * H > 65535) return fail(LI_ERR_SHAPE, "grid too large");
   dim3 grid((unsigned)nblk, (unsigned)(B * H));
   dim3 block(8 * a.CH * a.nstreams);
-  tile_pool_kernel<<<grid, block, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  const size_t smem = (size_t)8 * a.D * 8 + (size_t)a.bs * 4;
+  tile_pool_kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return cuda_status(cudaGetLastError(), "tile_pool_kernel launch");
 }
 
@@ -284,7 +287,7 @@ extern "C" li_status li_tile_pool(const li_view4* src0, const li_view4* src1, co
     a.src[1] = static_cast<const uint8_t*>(src1->data);
     a.s_b[1] = src1->stride[0]; a.s_h[1] = src1->stride[1]; a.s_l[1] = src1->stride[2];
   }
-  if (8 * a.CH * a.nstreams > 1024) return fail(LI_ERR_UNSUPPORTED, "D too large for the tiling kernel");
+  if (8 * a.CH * a.nstreams > 512) return fail(LI_ERR_UNSUPPORTED, "D too large for the tiling kernel");
   a.dst_off = dst_block_offset;
   a.pool_off = pool_block_offset;
   if (li_status st = fill_dst(a, 0, dst0, B, H, D, dtype, nblk + dst_block_offset, "dst0")) return st;
@@ -325,7 +328,7 @@ extern "C" li_status li_text_blocks(const li_view4* src0, const li_view4* src1, 
     a.src[1] = static_cast<const uint8_t*>(src1->data);
     a.s_b[1] = src1->stride[0]; a.s_h[1] = src1->stride[1]; a.s_l[1] = src1->stride[2];
   }
-  if (8 * a.CH * a.nstreams > 1024) return fail(LI_ERR_UNSUPPORTED, "D too large for the tiling kernel");
+  if (8 * a.CH * a.nstreams > 512) return fail(LI_ERR_UNSUPPORTED, "D too large for the tiling kernel");
   const int64_t nblk = ceil_div(N, bs);
   if (li_status st = fill_dst(a, 0, dst0, B, H, D, dtype, nblk, "dst0")) return st;
   if (li_status st = fill_dst(a, 1, dst1, B, H, D, dtype, nblk, "dst1")) return st;

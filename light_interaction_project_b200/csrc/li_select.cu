@@ -1,9 +1,11 @@
 // Block selection: pooled-score GEMM, protection bias, top-k, sorted emit.
 //
-// One CTA (8 warps) handles R <= 8 query rows of one (b, h). The query rows
-// and then the key rows, 32 at a time, are staged in shared memory as floats
-// with coalesced 16-byte loads ('cosine' normalises them there). Warp r forms
-// the dot products of query row r with the 32 staged key rows, one per lane.
+// One CTA (4 warps) handles R <= 4 query rows of one (b, h). The query rows
+// and then the key rows, 32 at a time, are staged in shared memory as doubles
+// with coalesced 16-byte loads ('cosine' normalises them there; the pipeline
+// normalises pools once with li_normalize_rows and selects with the plain dot
+// product instead). Warp r forms the dot products of query row r with the 32
+// staged key rows, one per lane.
 // Dot products and squared norms are exact-product fp64 sums (four interleaved
 // partial sums over d, combined in order), rounded once to fp32 and then to
 // the dtype; scalar multiplies/adds are single fp32 operations rounded to the
@@ -24,7 +26,7 @@
 namespace li {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxD = 256;
 constexpr size_t kSmemBudget = 160 * 1024;
@@ -60,7 +62,8 @@ __device__ __forceinline__ uint32_t radix_key(float v, int dt) {
 
 // Four interleaved fp64 partial sums of exact products, combined in order —
 // the summation order the CPU oracle restates.
-__device__ __forceinline__ double dot4(const float* x, const float* y, int D) {
+template <typename T>
+__device__ __forceinline__ double dot4(const T* x, const T* y, int D) {
   double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
   for (int d = 0; d < D; d += 4) {
     p0 = fma((double)x[d], (double)y[d], p0);
@@ -71,23 +74,29 @@ __device__ __forceinline__ double dot4(const float* x, const float* y, int D) {
   return ((p0 + p1) + p2) + p3;
 }
 
-// 16-byte chunk of a pooled row -> floats (exact widening).
-__device__ __forceinline__ void widen_chunk(const uint4& v, int dt, float* dst) {
+// 16-byte chunk of a pooled row -> doubles (exact widening).
+__device__ __forceinline__ void widen_chunk(const uint4& v, int dt, double* dst) {
   const int epc = dt == LI_DTYPE_FP32 ? 4 : 8;
-  for (int e = 0; e < epc; ++e) dst[e] = chunk_elem(v, e, dt);
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if (e < epc) dst[e] = chunk_elem_f64(v, e, dt);
 }
 
 constexpr int kChunkRows = 32;
 
+// Normalisation of F.normalize on a staged row (dtype values held as doubles).
+__device__ __forceinline__ void normalize_row(double* x, int D, int dt, float eps) {
+  const float den = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(dot4(x, x, D))), dt), eps);
+  for (int d = 0; d < D; ++d) x[d] = (double)round_dt(__fdiv_rn((float)x[d], den), dt);
+}
+
 template <int R>
 __global__ void __launch_bounds__(kThreads) select_kernel(const SelArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const int pitch = a.D + 1;                                   // bank-conflict-free row pitch
-  float* qs = reinterpret_cast<float*>(smem);                   // [R][pitch]
-  float* ks = qs + R * pitch;                                   // [kChunkRows][pitch]
-  float* kden = ks + kChunkRows * pitch;                        // [kChunkRows]
-  float* qden = kden + kChunkRows;                              // [R]
-  uint32_t* keys = reinterpret_cast<uint32_t*>(qden + R);       // [R][Nk]
+  const int pitch = a.D + 1;                                    // doubles; odd pitch spreads banks
+  double* qs = reinterpret_cast<double*>(smem);                 // [R][pitch]
+  double* ks = qs + R * pitch;                                  // [kChunkRows][pitch]
+  uint32_t* keys = reinterpret_cast<uint32_t*>(ks + kChunkRows * pitch);  // [R][Nk]
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
   const int q0 = blockIdx.x * R;
@@ -107,17 +116,7 @@ __global__ void __launch_bounds__(kThreads) select_kernel(const SelArgs a) {
     widen_chunk(v, a.dtype, qs + r * pitch + c * epc);
   }
   __syncthreads();
-  if (cosine) {
-    if (tid < R) {
-      const float* x = qs + tid * pitch;
-      qden[tid] = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(dot4(x, x, a.D))), a.dtype), a.eps);
-    }
-    __syncthreads();
-    for (int i = tid; i < R * a.D; i += kThreads) {
-      const int r = i / a.D, d = i % a.D;
-      qs[r * pitch + d] = round_dt(__fdiv_rn(qs[r * pitch + d], qden[r]), a.dtype);
-    }
-  }
+  if (cosine && tid < nrows) normalize_row(qs + tid * pitch, a.D, a.dtype, a.eps);
 
   const uint8_t* kbase = a.kp + (b * a.k_b + h * a.k_h) * es;
   const int warp = tid / 32, lane = tid % 32;
@@ -131,18 +130,10 @@ __global__ void __launch_bounds__(kThreads) select_kernel(const SelArgs a) {
     }
     __syncthreads();
     if (cosine) {
-      if (tid < kChunkRows) {
-        const float* x = ks + tid * pitch;
-        kden[tid] = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(dot4(x, x, a.D))), a.dtype), a.eps);
-      }
-      __syncthreads();
-      for (int i = tid; i < kChunkRows * a.D; i += kThreads) {
-        const int r = i / a.D, d = i % a.D;
-        ks[r * pitch + d] = round_dt(__fdiv_rn(ks[r * pitch + d], kden[r]), a.dtype);
-      }
+      if (tid < kChunkRows) normalize_row(ks + tid * pitch, a.D, a.dtype, a.eps);
       __syncthreads();
     }
-    // Warp r forms the dot products of query row r with the 32 staged key rows.
+    // Warp w forms the dot products of its query rows with the 32 staged key rows.
     for (int r = warp; r < nrows; r += kWarps) {
       const int j = c0 + lane;
       if (j >= a.Nk) continue;
@@ -206,6 +197,128 @@ __global__ void __launch_bounds__(kThreads) select_kernel(const SelArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two-kernel form (with a workspace): scores over a (row group, key chunk, b*h)
+// grid, then top-k per row. Same arithmetic as select_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kScoreRows = 8;    // query rows per CTA (two groups of four)
+constexpr int kScoreKeys = 64;   // key rows per CTA
+
+__device__ __forceinline__ float finish_score(const SelArgs& a, double acc, int b, int h, int qi, int j) {
+  float s = round_dt(__double2float_rn(acc), a.dtype);
+  if (a.metric == LI_METRIC_SCALED_DOT) s = round_dt(__fmul_rn(s, a.scale), a.dtype);
+  if (a.bias) s = round_dt(__fadd_rn(s, a.bias[b * a.x_b + h * a.x_h + qi * a.x_q + (int64_t)j * a.x_k]), a.dtype);
+  if (a.mode == LI_SELECT_DECODE) {
+    if (j >= a.Nk - a.n_prot) s = round_dt(__fadd_rn(s, a.big), a.dtype);
+  } else {
+    const int gq = qi + a.q_off;
+    const int hw = a.g_nh * a.g_nw;
+    const int tq = gq / hw, hq = (gq % hw) / a.g_nw, wq = gq % a.g_nw;
+    const int tk = j / hw, hk = (j % hw) / a.g_nw, wk = j % a.g_nw;
+    const int dist = abs(tq - tk) + abs(hq - hk) + abs(wq - wk);
+    s = round_dt(__fadd_rn(s, dist <= 1 ? a.big : 0.0f), a.dtype);
+  }
+  return s;
+}
+
+__global__ void __launch_bounds__(128) score_kernel(const SelArgs a, uint32_t* __restrict__ keys) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int pitch = a.D + 1;
+  double* qs = reinterpret_cast<double*>(smem);            // [kScoreRows][pitch]
+  double* ks = qs + kScoreRows * pitch;                    // [kScoreKeys][pitch]
+  const int bh = blockIdx.z, b = bh / a.H, h = bh % a.H;
+  const int q0 = blockIdx.x * kScoreRows, j0 = blockIdx.y * kScoreKeys;
+  const int nrows = min(kScoreRows, a.Nq - q0), nkeys = min(kScoreKeys, a.Nk - j0);
+  const int tid = threadIdx.x;
+  const int es = a.dtype == LI_DTYPE_FP32 ? 4 : 2, epc = 16 / es, CH = a.D / epc;
+  for (int i = tid; i < kScoreRows * CH; i += 128) {
+    const int r = i / CH, c = i % CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nrows) v = __ldg(reinterpret_cast<const uint4*>(a.qp + (b * a.q_b + h * a.q_h + (int64_t)(q0 + r) * a.q_n) * es) + c);
+    widen_chunk(v, a.dtype, qs + r * pitch + c * epc);
+  }
+  for (int i = tid; i < kScoreKeys * CH; i += 128) {
+    const int r = i / CH, c = i % CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nkeys) v = __ldg(reinterpret_cast<const uint4*>(a.kp + (b * a.k_b + h * a.k_h + (int64_t)(j0 + r) * a.k_n) * es) + c);
+    widen_chunk(v, a.dtype, ks + r * pitch + c * epc);
+  }
+  __syncthreads();
+  if (a.metric == LI_METRIC_COSINE) {
+    if (tid < nrows) normalize_row(qs + tid * pitch, a.D, a.dtype, a.eps);
+    if (tid >= 64 && tid - 64 < nkeys) normalize_row(ks + (tid - 64) * pitch, a.D, a.dtype, a.eps);
+    __syncthreads();
+  }
+  // Thread (g, jj): key jj against query rows 4g..4g+3, four partial sums each.
+  const int jj = tid % kScoreKeys, g = tid / kScoreKeys;
+  if (jj >= nkeys) return;
+  const double* kr = ks + jj * pitch;
+  const double* q0r = qs + (4 * g) * pitch;
+  double acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[r][u] = 0.0;
+  for (int d = 0; d < a.D; d += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const double kv = kr[d + u];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r][u] = fma(q0r[r * pitch + d + u], kv, acc[r][u]);
+    }
+  }
+  const int j = j0 + jj;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int lr = 4 * g + r;
+    if (lr >= nrows) break;
+    const int qi = q0 + lr;
+    const double dot = ((acc[r][0] + acc[r][1]) + acc[r][2]) + acc[r][3];
+    const float s = finish_score(a, dot, b, h, qi, j);
+    keys[((int64_t)bh * a.Nq + qi) * a.Nk + j] = radix_key(s, a.dtype);
+    if (a.rank) a.rank[b * a.r_b + h * a.r_h + qi * a.r_q + (int64_t)j * a.r_k] = s;
+  }
+}
+
+// One warp per query row: top-k of the precomputed radix keys, emitted sorted.
+__global__ void __launch_bounds__(128) topk_kernel(const SelArgs a, const uint32_t* __restrict__ keys) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qi = blockIdx.x * 4 + warp, bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  if (qi >= a.Nq) return;
+  uint32_t* rk = reinterpret_cast<uint32_t*>(smem) + warp * a.Nk;
+  const uint32_t* src = keys + ((int64_t)bh * a.Nq + qi) * a.Nk;
+  for (int j = lane; j < a.Nk; j += 32) rk[j] = src[j];
+  __syncwarp();
+  const uint64_t low_mask = (1ull << a.idx_bits) - 1ull;
+  const int k = a.k_budget;
+  uint64_t thr = 0;
+  if (k > 0 && k < a.Nk) {
+    for (int bit = a.key_bits + a.idx_bits - 1; bit >= 0; --bit) {
+      const uint64_t cand = thr | (1ull << bit);
+      int c = 0;
+      for (int j = lane; j < a.Nk; j += 32) c += (((uint64_t)rk[j] << a.idx_bits) | (low_mask - (uint64_t)j)) >= cand;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+      if (c >= k) thr = cand;
+    }
+  }
+  int32_t* out = a.idx + b * a.i_b + h * a.i_h + (int64_t)qi * a.i_q;
+  for (int t = lane; t < a.ntxt; t += 32) out[(int64_t)t * a.i_s] = t;
+  int pos = 0;
+  if (k > 0) {
+    for (int base = 0; base < a.Nk; base += 32) {
+      const int j = base + lane;
+      bool sel = false;
+      if (j < a.Nk) sel = (k >= a.Nk) || ((((uint64_t)rk[j] << a.idx_bits) | (low_mask - (uint64_t)j)) >= thr);
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, sel);
+      if (sel) out[(int64_t)(a.ntxt + pos + __popc(m & ((1u << lane) - 1u))) * a.i_s] = j + a.ntxt;
+      pos += __popc(m);
+    }
+  }
+  if (lane == 0) a.cnt[b * a.c_b + h * a.c_h + (int64_t)qi * a.c_q] = a.ntxt + k;
+}
+
 li_status budget_of(const li_select_params* p, int64_t nq, int64_t nk, int32_t* ntxt, int32_t* kb,
                     int32_t* nprot) {
   if (!p) return fail(LI_ERR_INVALID_ARG, "params required");
@@ -266,6 +379,63 @@ cudaError_t launch_select(const SelArgs& a, dim3 grid, size_t smem, cudaStream_t
 
 using namespace li;
 
+namespace li {
+namespace {
+// Row-wise F.normalize of pooled rows, exactly as the selection kernel does it
+// for 'cosine': 64 rows per CTA staged as doubles, one thread per row.
+__global__ void __launch_bounds__(64) normalize_kernel(const uint8_t* x, int64_t x_b, int64_t x_h, int64_t x_n,
+                                                        uint8_t* y, int64_t y_b, int64_t y_h, int64_t y_n, int H,
+                                                        int N, int D, int dtype, float eps) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int pitch = D + 1;
+  double* rows = reinterpret_cast<double*>(smem);   // [64][pitch]
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int n0 = blockIdx.x * 64;
+  const int es = dtype == LI_DTYPE_FP32 ? 4 : 2, epc = 16 / es, CH = D / epc;
+  for (int i = threadIdx.x; i < 64 * CH; i += 64) {
+    const int r = i / CH, c = i % CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n0 + r < N) v = __ldg(reinterpret_cast<const uint4*>(x + (b * x_b + h * x_h + (int64_t)(n0 + r) * x_n) * es) + c);
+    widen_chunk(v, dtype, rows + r * pitch + c * epc);
+  }
+  __syncthreads();
+  if (n0 + (int)threadIdx.x < N) normalize_row(rows + threadIdx.x * pitch, D, dtype, eps);
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * D; i += 64) {
+    const int r = i / D, d = i % D;
+    if (n0 + r < N) store_dt(y + (b * y_b + h * y_h + (int64_t)(n0 + r) * y_n) * es, d, (float)rows[r * pitch + d], dtype);
+  }
+}
+}  // namespace
+}  // namespace li
+
+extern "C" li_status li_normalize_rows(const li_view4* x, li_view4* y, void* stream) {
+  if (!x || !y) return fail(LI_ERR_INVALID_ARG, "x and y are required");
+  const int64_t B = x->shape[0], H = x->shape[1], N = x->shape[2], D = x->shape[3];
+  const int dt = x->dtype;
+  if (li_status st = check_vec_view(x->data, x->stride, 4, dt, D, "x")) return st;
+  if (li_status st = check_vec_view(y->data, y->stride, 4, y->dtype, D, "y")) return st;
+  if (y->dtype != dt) return fail(LI_ERR_INVALID_ARG, "y dtype differs from x");
+  for (int i = 0; i < 4; ++i)
+    if (y->shape[i] != x->shape[i]) return fail(LI_ERR_SHAPE, "y shape differs from x");
+  if (D > kMaxD) return fail(LI_ERR_UNSUPPORTED, "D=%lld", (long long)D);
+  if (B * H == 0 || N == 0) return LI_OK;
+  const float eps = dt == LI_DTYPE_FP32 ? 1e-12f
+                  : dt == LI_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(1e-12f))
+                                        : __half2float(__float2half_rn(1e-12f));
+  const size_t smem = (size_t)64 * (D + 1) * 8;
+  static bool configured = false;
+  if (!configured) {
+    if (li_status st = cuda_status(cudaFuncSetAttribute(normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)(64 * (kMaxD + 1) * 8)), "normalize smem attribute")) return st;
+    configured = true;
+  }
+  normalize_kernel<<<dim3((unsigned)ceil_div(N, 64), (unsigned)(B * H)), 64, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(x->data), x->stride[0], x->stride[1], x->stride[2], static_cast<uint8_t*>(y->data),
+      y->stride[0], y->stride[1], y->stride[2], (int)H, (int)N, (int)D, dt, eps);
+  return cuda_status(cudaGetLastError(), "normalize_kernel launch");
+}
+
 extern "C" li_status li_select_budget(const li_select_params* p, int64_t n_q_blocks, int64_t n_k_blocks,
                                       int32_t* n_text_blocks, int32_t* budget) {
   int32_t nprot;
@@ -273,11 +443,15 @@ extern "C" li_status li_select_budget(const li_select_params* p, int64_t n_q_blo
   return budget_of(p, n_q_blocks, n_k_blocks, n_text_blocks, budget, &nprot);
 }
 
-extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_pool,
-                                      const li_select_params* p, const li_view4* score_bias,
-                                      li_index_view* out, li_view4* rank_out, void* stream) {
+namespace li {
+namespace {
+// Validates the arguments of a selection and fills the kernel arguments.
+li_status prepare_select(const li_view4* q_pool, const li_view4* k_pool, const li_select_params* p,
+                         const li_view4* score_bias, li_index_view* out, li_view4* rank_out, SelArgs& a,
+                         int64_t& B, int64_t& H) {
   if (!q_pool || !k_pool || !p) return fail(LI_ERR_INVALID_ARG, "q_pool, k_pool and params are required");
-  const int64_t B = q_pool->shape[0], H = q_pool->shape[1], Nq = q_pool->shape[2], D = q_pool->shape[3];
+  B = q_pool->shape[0]; H = q_pool->shape[1];
+  const int64_t Nq = q_pool->shape[2], D = q_pool->shape[3];
   const int64_t Nk = k_pool->shape[2];
   const int dt = q_pool->dtype;
   if (!valid_dtype(dt) || k_pool->dtype != dt) return fail(LI_ERR_INVALID_ARG, "pool dtypes must match");
@@ -285,7 +459,7 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
     return fail(LI_ERR_SHAPE, "k_pool shape does not match q_pool");
   if (li_status st = check_vec_view(q_pool->data, q_pool->stride, 4, dt, D, "q_pool")) return st;
   if (li_status st = check_vec_view(k_pool->data, k_pool->stride, 4, dt, D, "k_pool")) return st;
-  if (D <= 0 || D > kMaxD) return fail(LI_ERR_UNSUPPORTED, "D=%lld", (long long)D);
+  if (D <= 0 || D > kMaxD || D % 4) return fail(LI_ERR_UNSUPPORTED, "D=%lld", (long long)D);
   if (p->metric < LI_METRIC_COSINE || p->metric > LI_METRIC_DOT) return fail(LI_ERR_INVALID_ARG, "metric");
   int32_t ntxt, kb, nprot;
   if (li_status st = budget_of(p, Nq, Nk, &ntxt, &kb, &nprot)) return st;
@@ -297,8 +471,6 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
                   (long long)(p->q_block_offset + Nq), (long long)Nk);
   }
   if (Nk > (1 << 24)) return fail(LI_ERR_UNSUPPORTED, "too many key blocks");
-  if (B * H == 0 || Nq == 0) return LI_OK;
-  SelArgs a;
   memset(&a, 0, sizeof(a));
   a.qp = static_cast<const uint8_t*>(q_pool->data);
   a.q_b = q_pool->stride[0]; a.q_h = q_pool->stride[1]; a.q_n = q_pool->stride[2];
@@ -341,11 +513,18 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
           : dt == LI_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(one_e6))
                                 : __half2float(__float2half_rn(one_e6));
   }
-  // Rows per CTA: as many (<= 8) as fit the shared-memory budget.
+  return LI_OK;
+}
+
+int64_t select_ws_bytes(int64_t B, int64_t H, int64_t Nq, int64_t Nk) { return B * H * Nq * Nk * 4; }
+
+// Single-kernel selection (no workspace).
+li_status launch_single(SelArgs& a, int64_t B, int64_t H, cudaStream_t s) {
+  const int64_t D = a.D, Nk = a.Nk, Nq = a.Nq;
   auto smem_of = [&](int r) {
-    return (size_t)4 * ((size_t)r * (D + 1) + (size_t)kChunkRows * (D + 1) + kChunkRows + r + (size_t)r * Nk);
+    return (size_t)8 * ((size_t)r * (D + 1) + (size_t)kChunkRows * (D + 1)) + (size_t)4 * r * Nk;
   };
-  int R = 8;
+  int R = 4;
   while (R > 1 && smem_of(R) > kSmemBudget) R >>= 1;
   if (smem_of(R) > kSmemBudget)
     return fail(LI_ERR_UNSUPPORTED, "%lld key blocks exceed the selection kernel's shared memory", (long long)Nk);
@@ -353,15 +532,57 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
   a.R = R;
   const size_t smem = smem_of(R);
   dim3 grid((unsigned)ceil_div(Nq, R), (unsigned)(B * H));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (R) {
-    case 8: e = launch_select<8>(a, grid, smem, s); break;
     case 4: e = launch_select<4>(a, grid, smem, s); break;
     case 2: e = launch_select<2>(a, grid, smem, s); break;
     default: e = launch_select<1>(a, grid, smem, s); break;
   }
   return cuda_status(e, "select_kernel launch");
+}
+
+// Two-kernel selection through `keys` (B*H*Nq*Nk uint32).
+li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStream_t s) {
+  static bool configured = false;
+  if (!configured) {
+    if (li_status st = cuda_status(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)((kScoreRows + kScoreKeys) * (kMaxD + 1) * 8)),
+                                   "score_kernel smem attribute")) return st;
+    if (li_status st = cuda_status(cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)kSmemBudget), "topk_kernel smem attribute")) return st;
+    configured = true;
+  }
+  const size_t smem1 = (size_t)(kScoreRows + kScoreKeys) * (a.D + 1) * 8;
+  score_kernel<<<dim3((unsigned)ceil_div(a.Nq, kScoreRows), (unsigned)ceil_div(a.Nk, kScoreKeys), (unsigned)(B * H)),
+                 128, smem1, s>>>(a, keys);
+  if (li_status st = cuda_status(cudaGetLastError(), "score_kernel launch")) return st;
+  const size_t smem2 = (size_t)4 * a.Nk * 4;
+  topk_kernel<<<dim3((unsigned)ceil_div(a.Nq, 4), (unsigned)(B * H)), 128, smem2, s>>>(a, keys);
+  return cuda_status(cudaGetLastError(), "topk_kernel launch");
+}
+}  // namespace
+}  // namespace li
+
+extern "C" li_status li_select_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks, int64_t n_k_blocks,
+                                               int64_t* bytes) {
+  if (!bytes) return fail(LI_ERR_INVALID_ARG, "bytes is required");
+  *bytes = (size_t)16 * n_k_blocks <= kSmemBudget ? select_ws_bytes(batch, heads, n_q_blocks, n_k_blocks) : 0;
+  return LI_OK;
+}
+
+extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_pool,
+                                      const li_select_params* p, const li_view4* score_bias,
+                                      li_index_view* out, li_view4* rank_out, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
+  SelArgs a;
+  int64_t B, H;
+  if (li_status st = prepare_select(q_pool, k_pool, p, score_bias, out, rank_out, a, B, H)) return st;
+  if (B * H == 0 || a.Nq == 0) return LI_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t need = select_ws_bytes(B, H, a.Nq, a.Nk);
+  if (workspace && workspace_bytes >= need && (size_t)16 * a.Nk <= kSmemBudget && aligned16(workspace))
+    return launch_two(a, B, H, static_cast<uint32_t*>(workspace), s);
+  return launch_single(a, B, H, s);
 }
 
 // ---------------------------------------------------------------------------

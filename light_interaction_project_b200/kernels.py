@@ -146,9 +146,13 @@ def select_budget(p: L.SelectParams, nq: int, nk: int) -> Tuple[int, int]:
 
 
 def select_blocks(q_pool: torch.Tensor, k_pool: torch.Tensor, p: L.SelectParams,
-                  score_bias: Optional[torch.Tensor] = None, return_rank: bool = False):
+                  score_bias: Optional[torch.Tensor] = None, return_rank: bool = False,
+                  use_workspace: bool = True):
     """Block selection on pooled tensors — ``li_select_blocks``. Returns
-    ``(indices, counts)`` (and the fp32 ranking scores with ``return_rank``)."""
+    ``(indices, counts)`` (and the fp32 ranking scores with ``return_rank``).
+    With ``use_workspace`` the scores and the top-k run as two wide kernels
+    through a scratch buffer from torch's allocator; without it one kernel."""
+    import ctypes
     lib = L.load()
     B, H, nq, _ = q_pool.shape
     nk = k_pool.shape[2]
@@ -161,11 +165,27 @@ def select_blocks(q_pool: torch.Tensor, k_pool: torch.Tensor, p: L.SelectParams,
     if score_bias is not None:
         score_bias = score_bias.to(torch.float32).expand(B, H, nq, nk)
         bias_v = L.view4(score_bias, "score_bias")
+    ws, wsb = None, 0
+    if use_workspace:
+        nb = ctypes.c_int64()
+        L.check(lib.li_select_workspace_bytes(B, H, nq, nk, ctypes.byref(nb)), "li_select_workspace_bytes")
+        if nb.value:
+            ws, wsb = torch.empty(nb.value, dtype=torch.uint8, device=dev), nb.value
     iv = L.index_view(idx, cnt)
     rv = L.view4(rank, "rank") if rank is not None else None
     L.check(lib.li_select_blocks(L.ptr(L.view4(q_pool, "q_pool")), L.ptr(L.view4(k_pool, "k_pool")), L.ptr(p),
-                                 L.ptr(bias_v), L.ptr(iv), L.ptr(rv), L.stream_ptr(dev)), "li_select_blocks")
+                                 L.ptr(bias_v), L.ptr(iv), L.ptr(rv), ws.data_ptr() if ws is not None else None,
+                                 int(wsb), L.stream_ptr(dev)), "li_select_blocks")
     return (idx, cnt, rank) if return_rank else (idx, cnt)
+
+
+def normalize_rows(x: torch.Tensor) -> torch.Tensor:
+    """``F.normalize(x, dim=-1)`` of pooled rows with the selection's rounding — ``li_normalize_rows``."""
+    lib = L.load()
+    y = torch.empty_like(x)
+    L.check(lib.li_normalize_rows(L.ptr(L.view4(x, "x")), L.ptr(L.view4(y, "y")), L.stream_ptr(x.device)),
+            "li_normalize_rows")
+    return y
 
 
 def rank_blocks(rank_scores: torch.Tensor, score_dtype: torch.dtype, k: int, text_len: int, bs: int):

@@ -59,7 +59,13 @@ def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode:
     q_pool = K.pool_blocks(q, T_q, LH, LW, tile)
     k_pool = K.pool_blocks(k_vis, T_k, LH, LW, tile)
     mark("prep_end")
-    p = K.select_params(mode, params.get("sim_metric", default_metric), tile, gq, gk, text_len,
+    metric = params.get("sim_metric", default_metric)
+    if metric == "cosine":
+        # Cosine similarity is the plain dot product of the normalised pools
+        # (same rounding chain); normalising once here keeps it out of the
+        # selection kernel's inner loop.
+        q_pool, k_pool, metric = K.normalize_rows(q_pool), K.normalize_rows(k_pool), "dot"
+    p = K.select_params(mode, metric, tile, gq, gk, text_len,
                         recent_protect=params.get("recent_protect", 0),
                         topk_ratio=params.get("topk_ratio", 1.0) if ratio is None else ratio,
                         min_budget=min_budget, q_block_offset=q_block_offset or 0)

@@ -143,3 +143,41 @@ def test_rank_matches_torch_cuda_topk(cuda_ok, dtype):
     assert torch.equal(idx[..., :2].cpu(), torch.arange(2, dtype=torch.int32).expand(B, H, nq, 2))
     assert torch.equal(idx[..., 2:].long().cpu() - 2, ti.cpu())
     assert (cnt == 2 + k).all()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "fp32"])
+def test_normalize_rows_and_cosine_equals_dot_of_normalised(cuda_ok, dtype):
+    """li_normalize_rows is bit-exact with the oracle's F.normalize, and cosine
+    selection equals plain-dot selection of the normalised pools (the pipeline's path)."""
+    B, H, nq, nk, D = 1, 3, 56, 280, 128 if dtype != "fp32" else 64
+    qp, _ = rand((B, H, nq, D), 77, dtype, scale=0.3)
+    kp, _ = rand((B, H, nk, D), 78, dtype, scale=0.3)
+    tq, tk = to_gpu(qp, dtype), to_gpu(kp, dtype)
+    nqn = K.normalize_rows(tq)
+    np.testing.assert_array_equal(to_np(nqn), O.normalize_rows(qp, dtype))
+    gk = (5, 8, 7)
+    p_cos = K.select_params(L.SELECT_BIDIR, "cosine", (4, 4, 8), gk, gk, 0, 0, 0.3, 7, nk - nq)
+    p_dot = K.select_params(L.SELECT_BIDIR, "dot", (4, 4, 8), gk, gk, 0, 0, 0.3, 7, nk - nq)
+    i1, c1, r1 = K.select_blocks(tq, tk, p_cos, return_rank=True)
+    i2, c2, r2 = K.select_blocks(nqn, K.normalize_rows(tk), p_dot, return_rank=True)
+    assert torch.equal(i1, i2) and torch.equal(c1, c2) and torch.equal(r1, r2)
+
+
+@pytest.mark.parametrize("mode", ["decode", "bidir"])
+def test_two_kernel_and_single_kernel_paths_agree(cuda_ok, mode):
+    """With a workspace the scores and the top-k run as two kernels; without,
+    as one. Both follow the same arithmetic: identical indices and scores."""
+    dtype = "bf16"
+    B, H, D = 1, 4, 128
+    gk = (17, 8, 7)
+    nk = int(np.prod(gk))
+    nq = 56
+    qp, kp = _pools(55, B, H, nq, nk, D, dtype, None)
+    tq, tk = to_gpu(qp, dtype), to_gpu(kp, dtype)
+    if mode == "decode":
+        p = K.select_params(L.SELECT_DECODE, "scaled_dot_product", (4, 4, 8), (1, 8, 7), gk, 5, 4, 0.25)
+    else:
+        p = K.select_params(L.SELECT_BIDIR, "cosine", (4, 4, 8), gk, gk, 0, 0, 0.25, 7, nk - nq)
+    i1, c1, r1 = K.select_blocks(tq, tk, p, return_rank=True, use_workspace=True)
+    i2, c2, r2 = K.select_blocks(tq, tk, p, return_rank=True, use_workspace=False)
+    assert torch.equal(i1, i2) and torch.equal(c1, c2) and torch.equal(r1, r2)
