@@ -171,6 +171,27 @@ li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_pool,
 li_status li_select_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks, int64_t n_k_blocks,
                                     int64_t* bytes);
 
+/* Size of the scratch array behind li_select_blocks_static. */
+#define LI_SELECT_STATIC_SCRATCH_BYTES (8ll << 20)
+
+/* li_select_blocks' two-kernel path with its scratch in a fixed array of the
+ * library's own global memory (LI_SELECT_STATIC_SCRATCH_BYTES), so the call
+ * allocates nothing: for hosts with no device allocator to hand a workspace
+ * from. No reference counterpart — the reference always allocates its score
+ * tensors through torch.
+ * - Same arguments and results (bit for bit) as li_select_blocks with a
+ *   workspace; nothing in the scratch has to start at zero.
+ * - Shapes needing more than batch*heads*n_q_blocks*n_k_blocks*4 =
+ *   LI_SELECT_STATIC_SCRATCH_BYTES bytes return LI_ERR_UNSUPPORTED.
+ * - The first call on each device looks the array up (and may load the
+ *   library's module); make it, with that device current, before any stream
+ *   capture.
+ * - One array per device: calls that may run at the same time on one device
+ *   (different streams, or host threads without ordering) race on it. */
+li_status li_select_blocks_static(const li_view4* q_pool, const li_view4* k_pool,
+                                  const li_select_params* p, const li_view4* score_bias,
+                                  li_index_view* out, li_view4* rank_out, void* stream);
+
 /* Row-wise F.normalize (dim=-1) of pooled rows, with the selection kernel's
  * exact rounding chain: y = dtype(x / max(dtype(sqrt(fp32(sum x^2))), dtype(1e-12))).
  * Cosine selection equals the plain-dot selection of normalised pools, so the

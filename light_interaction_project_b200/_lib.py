@@ -78,6 +78,8 @@ SIGNATURES = {
     "li_select_blocks": ([POINTER(View4), POINTER(View4), POINTER(SelectParams), POINTER(View4), POINTER(IndexView),
                           POINTER(View4), c_void_p, c_int64, c_void_p], c_int32),
     "li_select_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, POINTER(c_int64)], c_int32),
+    "li_select_blocks_static": ([POINTER(View4), POINTER(View4), POINTER(SelectParams), POINTER(View4),
+                                 POINTER(IndexView), POINTER(View4), c_void_p], c_int32),
     "li_normalize_rows": ([POINTER(View4), POINTER(View4), c_void_p], c_int32),
     "li_rank_blocks": ([POINTER(View4), c_int32, c_int32, c_int32, c_int32, POINTER(IndexView), c_void_p], c_int32),
     "li_sparse_attn_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, c_int32, POINTER(c_int64)], c_int32),

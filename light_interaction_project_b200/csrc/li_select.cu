@@ -20,6 +20,7 @@
 // already sorted ascending, so no sort is needed.
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "li_common.cuh"
 
@@ -583,6 +584,69 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
   if (workspace && workspace_bytes >= need && (size_t)16 * a.Nk <= kSmemBudget && aligned16(workspace))
     return launch_two(a, B, H, static_cast<uint32_t*>(workspace), s);
   return launch_single(a, B, H, s);
+}
+
+// ---------------------------------------------------------------------------
+// Two-kernel selection through a scratch buffer the library owns.
+//
+// Some callers have no device allocator to hand a workspace from: a host
+// binding over the C ABI (cgo, JNI, ctypes) that links no torch, or a serving
+// loop that must not call cudaMalloc mid-step because it synchronises the
+// device and stalls every other stream. For them the sort keys of the
+// two-kernel path live in a fixed array in this module's global memory, which
+// is reserved when the module loads, so the call itself allocates nothing.
+// ---------------------------------------------------------------------------
+static_assert(LI_SELECT_STATIC_SCRATCH_BYTES % 4 == 0, "scratch holds 32-bit keys");
+// One 32-bit key per (b, h, query row, key block). The score kernel writes
+// every word the top-k kernel reads within the same call, so no part of it has
+// to start at zero and nothing carries over between calls.
+static __device__ __align__(256) uint32_t g_select_scratch[LI_SELECT_STATIC_SCRATCH_BYTES / 4];
+
+namespace li {
+namespace {
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+uint32_t* g_scratch_addr[kMaxScratchDevices];
+
+// Device address of g_select_scratch on the current device, looked up once per
+// device. The first lookup may load this module onto the device.
+li_status static_scratch(uint32_t** addr) {
+  int dev = 0;
+  if (li_status st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice")) return st;
+  if (dev < 0 || dev >= kMaxScratchDevices) return fail(LI_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    if (li_status st = cuda_status(cudaGetSymbolAddress(&p, g_select_scratch),
+                                   "cudaGetSymbolAddress(selection scratch)")) return st;
+    if (!p || !aligned16(p)) return fail(LI_ERR_CUDA, "selection scratch address is not 16-byte aligned");
+    g_scratch_addr[dev] = static_cast<uint32_t*>(p);
+  }
+  *addr = g_scratch_addr[dev];
+  return LI_OK;
+}
+}  // namespace
+}  // namespace li
+
+extern "C" li_status li_select_blocks_static(const li_view4* q_pool, const li_view4* k_pool,
+                                             const li_select_params* p, const li_view4* score_bias,
+                                             li_index_view* out, li_view4* rank_out, void* stream) {
+  SelArgs a;
+  int64_t B, H;
+  if (li_status st = prepare_select(q_pool, k_pool, p, score_bias, out, rank_out, a, B, H)) return st;
+  const int64_t need = select_ws_bytes(B, H, a.Nq, a.Nk);
+  if (need > LI_SELECT_STATIC_SCRATCH_BYTES)
+    return fail(LI_ERR_UNSUPPORTED,
+                "selection of %lld x %lld x %lld x %lld (batch x heads x query blocks x key blocks) needs %lld "
+                "bytes of scratch; the static buffer holds %lld (use li_select_blocks with a workspace)",
+                (long long)B, (long long)H, (long long)a.Nq, (long long)a.Nk, (long long)need,
+                (long long)LI_SELECT_STATIC_SCRATCH_BYTES);
+  if ((size_t)16 * a.Nk > kSmemBudget)
+    return fail(LI_ERR_UNSUPPORTED, "%lld key blocks exceed the top-k kernel's shared memory", (long long)a.Nk);
+  uint32_t* scratch = nullptr;
+  if (li_status st = static_scratch(&scratch)) return st;
+  if (B * H == 0 || a.Nq == 0) return LI_OK;
+  return launch_two(a, B, H, scratch, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------
