@@ -88,6 +88,10 @@ typedef struct li_grid3d {
 const char* li_version(void);
 /* Message of the last failed call on this host thread ("" if none). */
 const char* li_last_error(void);
+/* Kernels this process has launched through the library so far (all devices,
+ * all threads). A diagnostic with no reference counterpart: benchmarks read it
+ * before and after a timed region. */
+uint64_t li_kernel_launches(void);
 
 /* ---- (a1, a2, a3, a10) tiling + pooling + frame gather ------------------
  * Replaces launch_q_prep / _fused_q_prep_kernel

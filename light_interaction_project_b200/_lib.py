@@ -11,7 +11,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from ctypes import POINTER, Structure, c_char_p, c_double, c_float, c_int32, c_int64, c_uint32, c_void_p
+from ctypes import POINTER, Structure, c_char_p, c_double, c_float, c_int32, c_int64, c_uint32, c_uint64, c_void_p
 
 import torch
 
@@ -69,6 +69,7 @@ _lock = threading.Lock()
 SIGNATURES = {
     "li_version": ([], c_char_p),
     "li_last_error": ([], c_char_p),
+    "li_kernel_launches": ([], c_uint64),
     "li_tile_pool": ([POINTER(View4), POINTER(View4), c_void_p, Grid3d, POINTER(View5), POINTER(View5), c_int64,
                       POINTER(View4), c_int64, c_void_p], c_int32),
     "li_text_blocks": ([POINTER(View4), POINTER(View4), c_int32, POINTER(View5), POINTER(View5), c_void_p], c_int32),
@@ -111,6 +112,11 @@ def load(path: str = LIB_PATH):
 
 def last_error() -> str:
     return load().li_last_error().decode()
+
+
+def kernel_launches() -> int:
+    """Kernels this process has launched through the library so far."""
+    return int(load().li_kernel_launches())
 
 
 def check(status: int, what: str):

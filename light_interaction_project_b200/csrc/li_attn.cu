@@ -804,15 +804,14 @@ int64_t workspace_bytes(int64_t units, int64_t D) { return units * 128 * (D + 2)
 template <int D, int BS, bool F16>
 li_status launch_t(const Params& prm, dim3 grid, cudaStream_t stream) {
   using L = Smem<D, BS>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D, BS, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::kBytes);
-    if (e != cudaSuccess) return cuda_status(e, "attention smem attribute");
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (li_status st = once_per_device(configured, [] {
+        return cuda_status(cudaFuncSetAttribute(attn_fwd_kernel<D, BS, F16>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes),
+                           "attention smem attribute");
+      })) return st;
   attn_fwd_kernel<D, BS, F16><<<grid, kThreads, L::kBytes, stream>>>(prm);
-  return cuda_status(cudaGetLastError(), "attention kernel launch");
+  return launched("attention kernel launch");
 }
 
 li_status launch(int D, int BS, bool f16, const Params& prm, dim3 grid, cudaStream_t s) {
@@ -968,7 +967,7 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
     }
     ca.q_len = q->shape[2];
     attn_combine_kernel<<<dim3((unsigned)nq, (unsigned)(B * H)), 128, 0, static_cast<cudaStream_t>(stream)>>>(ca);
-    if (li_status st = cuda_status(cudaGetLastError(), "attention combine launch")) return st;
+    if (li_status st = launched("attention combine launch")) return st;
   }
   return LI_OK;
 }

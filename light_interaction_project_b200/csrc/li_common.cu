@@ -7,6 +7,7 @@
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
 }
 
 namespace li {
@@ -24,6 +25,12 @@ li_status fail(li_status code, const char* fmt, ...) {
 li_status cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return LI_OK;
   return fail(LI_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+li_status launched(const char* what) {
+  if (li_status st = cuda_status(cudaGetLastError(), what)) return st;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return LI_OK;
 }
 
 li_status check_vec_view(const void* data, const int64_t* stride, int rank, int dtype,
@@ -46,3 +53,5 @@ li_status check_vec_view(const void* data, const int64_t* stride, int rank, int 
 extern "C" const char* li_version(void) { return "li_b200 0.1.0 (sm_100a)"; }
 
 extern "C" const char* li_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" uint64_t li_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -6,6 +6,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "li_b200.h"
 
 namespace li {
@@ -14,6 +16,9 @@ namespace li {
 li_status fail(li_status code, const char* fmt, ...);
 // LI_OK when `e` is cudaSuccess, else records the CUDA error string.
 li_status cuda_status(cudaError_t e, const char* what);
+// Checks the launch just issued (cudaGetLastError) and, when it was accepted,
+// adds one to the process-wide count li_kernel_launches() reports.
+li_status launched(const char* what);
 
 inline int dtype_size(int dt) { return dt == LI_DTYPE_FP32 ? 4 : 2; }
 inline bool valid_dtype(int dt) { return dt == LI_DTYPE_BF16 || dt == LI_DTYPE_FP16 || dt == LI_DTYPE_FP32; }
@@ -24,6 +29,20 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // multiple of 16 bytes, base 16-byte aligned.
 li_status check_vec_view(const void* data, const int64_t* stride, int rank, int dtype,
                          int64_t D, const char* name);
+
+// Kernel attributes (the dynamic shared-memory limit) belong to one device's
+// context. `done` holds one bit per device ordinal below 64 for one call site;
+// `setup` runs on the current device until it has succeeded there once.
+template <class F>
+li_status once_per_device(std::atomic<uint64_t>& done, F&& setup) {
+  int dev = 0;
+  if (li_status st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice")) return st;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t{1} << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return LI_OK;
+  if (li_status st = setup()) return st;
+  done.fetch_or(bit, std::memory_order_release);
+  return LI_OK;
+}
 
 // ---------------------------------------------------------------------------
 // Device-side rounding helpers (exact IEEE round-to-nearest-even).

@@ -244,7 +244,7 @@ li_status launch_tile(TileArgs& a, int64_t nblk, int64_t B, int64_t H, void* str
   dim3 block(8 * a.CH * a.nstreams);
   const size_t smem = (size_t)8 * a.D * 8 + (size_t)a.bs * 4;
   tile_pool_kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(a);
-  return cuda_status(cudaGetLastError(), "tile_pool_kernel launch");
+  return launched("tile_pool_kernel launch");
 }
 
 }  // namespace
@@ -362,7 +362,7 @@ extern "C" li_status li_untile(const li_view5* src, li_grid3d grid, li_view4* ds
   if (nblk == 0 || B * H == 0) return LI_OK;
   untile_kernel<<<dim3((unsigned)nblk, (unsigned)(B * H)), dim3(8 * a.CH), 0,
                   static_cast<cudaStream_t>(stream)>>>(a);
-  return cuda_status(cudaGetLastError(), "untile_kernel launch");
+  return launched("untile_kernel launch");
 }
 
 extern "C" li_status li_gather_frames(const li_view4* src, const int32_t* frame_ids, int32_t n_frames,
@@ -391,5 +391,5 @@ extern "C" li_status li_gather_frames(const li_view4* src, const int32_t* frame_
   if (n_frames == 0 || B * H == 0) return LI_OK;
   gather_frames_kernel<<<dim3((unsigned)n_frames, (unsigned)(B * H)), dim3(256), 0,
                          static_cast<cudaStream_t>(stream)>>>(a);
-  return cuda_status(cudaGetLastError(), "gather_frames_kernel launch");
+  return launched("gather_frames_kernel launch");
 }

@@ -363,16 +363,14 @@ li_status check_index_out(const li_index_view* o, int64_t B, int64_t H, int64_t 
 }
 
 template <int R>
-cudaError_t launch_select(const SelArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(select_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBudget);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+li_status launch_select(const SelArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};
+  if (li_status st = once_per_device(configured, [] {
+        return cuda_status(cudaFuncSetAttribute(select_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)kSmemBudget), "select_kernel smem attribute");
+      })) return st;
   select_kernel<R><<<grid, kThreads, smem, s>>>(a);
-  return cudaGetLastError();
+  return launched("select_kernel launch");
 }
 
 }  // namespace
@@ -425,16 +423,15 @@ extern "C" li_status li_normalize_rows(const li_view4* x, li_view4* y, void* str
                   : dt == LI_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(1e-12f))
                                         : __half2float(__float2half_rn(1e-12f));
   const size_t smem = (size_t)64 * (D + 1) * 8;
-  static bool configured = false;
-  if (!configured) {
-    if (li_status st = cuda_status(cudaFuncSetAttribute(normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)(64 * (kMaxD + 1) * 8)), "normalize smem attribute")) return st;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (li_status st = once_per_device(configured, [] {
+        return cuda_status(cudaFuncSetAttribute(normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)(64 * (kMaxD + 1) * 8)), "normalize smem attribute");
+      })) return st;
   normalize_kernel<<<dim3((unsigned)ceil_div(N, 64), (unsigned)(B * H)), 64, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(x->data), x->stride[0], x->stride[1], x->stride[2], static_cast<uint8_t*>(y->data),
       y->stride[0], y->stride[1], y->stride[2], (int)H, (int)N, (int)D, dt, eps);
-  return cuda_status(cudaGetLastError(), "normalize_kernel launch");
+  return launched("normalize_kernel launch");
 }
 
 extern "C" li_status li_select_budget(const li_select_params* p, int64_t n_q_blocks, int64_t n_k_blocks,
@@ -533,33 +530,30 @@ li_status launch_single(SelArgs& a, int64_t B, int64_t H, cudaStream_t s) {
   a.R = R;
   const size_t smem = smem_of(R);
   dim3 grid((unsigned)ceil_div(Nq, R), (unsigned)(B * H));
-  cudaError_t e;
   switch (R) {
-    case 4: e = launch_select<4>(a, grid, smem, s); break;
-    case 2: e = launch_select<2>(a, grid, smem, s); break;
-    default: e = launch_select<1>(a, grid, smem, s); break;
+    case 4: return launch_select<4>(a, grid, smem, s);
+    case 2: return launch_select<2>(a, grid, smem, s);
+    default: return launch_select<1>(a, grid, smem, s);
   }
-  return cuda_status(e, "select_kernel launch");
 }
 
 // Two-kernel selection through `keys` (B*H*Nq*Nk uint32).
 li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    if (li_status st = cuda_status(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)((kScoreRows + kScoreKeys) * (kMaxD + 1) * 8)),
-                                   "score_kernel smem attribute")) return st;
-    if (li_status st = cuda_status(cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)kSmemBudget), "topk_kernel smem attribute")) return st;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (li_status st = once_per_device(configured, [] {
+        if (li_status e = cuda_status(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                           (int)((kScoreRows + kScoreKeys) * (kMaxD + 1) * 8)),
+                                      "score_kernel smem attribute")) return e;
+        return cuda_status(cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)kSmemBudget), "topk_kernel smem attribute");
+      })) return st;
   const size_t smem1 = (size_t)(kScoreRows + kScoreKeys) * (a.D + 1) * 8;
   score_kernel<<<dim3((unsigned)ceil_div(a.Nq, kScoreRows), (unsigned)ceil_div(a.Nk, kScoreKeys), (unsigned)(B * H)),
                  128, smem1, s>>>(a, keys);
-  if (li_status st = cuda_status(cudaGetLastError(), "score_kernel launch")) return st;
+  if (li_status st = launched("score_kernel launch")) return st;
   const size_t smem2 = (size_t)4 * a.Nk * 4;
   topk_kernel<<<dim3((unsigned)ceil_div(a.Nq, 4), (unsigned)(B * H)), 128, smem2, s>>>(a, keys);
-  return cuda_status(cudaGetLastError(), "topk_kernel launch");
+  return launched("topk_kernel launch");
 }
 }  // namespace
 }  // namespace li
@@ -727,13 +721,12 @@ extern "C" li_status li_rank_blocks(const li_view4* rank_scores, int32_t score_d
   while ((1ll << ib) < Nk) ++ib;
   a.idx_bits = ib;
   a.key_bits = score_dtype == LI_DTYPE_FP32 ? 32 : 16;
-  static bool configured = false;
-  if (!configured) {
-    if (li_status st = cuda_status(cudaFuncSetAttribute(rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)kSmemBudget), "rank_kernel smem attribute")) return st;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (li_status st = once_per_device(configured, [] {
+        return cuda_status(cudaFuncSetAttribute(rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)kSmemBudget), "rank_kernel smem attribute");
+      })) return st;
   rank_kernel<<<dim3((unsigned)ceil_div(Nq, kWarps), (unsigned)(B * H)), kThreads, smem,
                 static_cast<cudaStream_t>(stream)>>>(a);
-  return cuda_status(cudaGetLastError(), "rank_kernel launch");
+  return launched("rank_kernel launch");
 }

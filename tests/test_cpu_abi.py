@@ -23,7 +23,7 @@ def lib():
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^(?:li_status|const char\*)\s+(li_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:li_status|const char\*|uint64_t)\s+(li_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_header_declares_every_bound_symbol():
