@@ -211,13 +211,14 @@ li_status li_rank_blocks(const li_view4* rank_scores, int32_t score_dtype, int32
                          int32_t text_len, int32_t bs, li_index_view* out, void* stream);
 
 /* ---- (a6, a7, a8) block-sparse attention forward ----------------------- */
-/* Split-KV workspace. When a launch has too few query blocks to fill the GPU,
- * each block's list is split over several CTAs that write fp32 partials
- * (O, row max, row sum) to a caller-provided device workspace, merged by a
- * second kernel. This returns the bytes the attention entry points will use
- * for that shape (0 = no split). A smaller or NULL workspace is allowed and
- * simply disables the split. No reference counterpart (the reference always
- * launches one program per 128 query rows). */
+/* Split-KV workspace. The attention runs one CTA per query block per SM; when
+ * the last wave of a launch would hold only a few blocks, the lists of those
+ * blocks are split over several CTAs that write fp32 partials (O, row max,
+ * row sum) to a caller-provided device workspace, merged by a second kernel.
+ * This returns the bytes the attention entry points will use for that shape
+ * (0 = no split; never more than one wave of partials). A smaller or NULL
+ * workspace is allowed and simply disables the split. No reference
+ * counterpart (the reference always launches one program per 128 query rows). */
 li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks,
                                          int64_t max_blocks_per_row, int32_t head_dim, int64_t* bytes);
 

@@ -69,10 +69,14 @@ struct __align__(64) Params {
   int32_t k_nh, k_nw, k_tt, k_th, k_tw;
   int32_t ntxt, n_kv, nq;
   int32_t smax;  // index-row width: counts are clamped to it
-  // Split-KV: CTA (qi, sp) handles list entries [S*sp/nsplit, S*(sp+1)/nsplit) and,
-  // when nsplit > 1, writes its unnormalised fp32 partial (O, m, l) to `part`
-  // (unit u = ((b*H + h)*nq + qi)*nsplit + sp: O at part + u*128*D, m and l
-  // after all O blocks) for attn_combine_kernel.
+  // Tail split. The 1-D grid lists the launch's query tiles t = (bl*H + h)*nq + qi;
+  // CTAs u < n_whole take tile u whole and store it. The remaining tiles are
+  // cut into nsplit pieces each: CTA u >= n_whole takes piece v = u - n_whole,
+  // i.e. list entries [S*sp/nsplit, S*(sp+1)/nsplit) of tile n_whole + v/nsplit
+  // (sp = v % nsplit), and writes its unnormalised fp32 partial (O at
+  // part + v*128*D; m, then l, after all part_units O blocks) for
+  // attn_combine_kernel.
+  int64_t n_whole;
   int32_t nsplit;
   float* part;
   int64_t part_units;
@@ -234,7 +238,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool f16, bool b_
 template <int D, int BS>
 struct Smem {
   static constexpr int kHalves = D / 64;
-  static constexpr int kNK = 2, kNV = 2;      // K and V ring stages (slot j % 2 = chain of block j)
+  // K and V ring stages: a K stage is refilled once the S MMA that read it has
+  // completed, a V stage once its PV MMA has.
+  static constexpr int kNK = 2, kNV = 2;
   static constexpr int kQHalf = 128 * 128;  // 128 rows of 128 bytes
   static constexpr int kKVHalf = BS * 128;
   static constexpr int kKVTile = kHalves * kKVHalf;
@@ -243,6 +249,12 @@ struct Smem {
   static constexpr int kOffV = kOffK + kNK * kKVTile;
   static constexpr int kOffX = kOffV + kNV * kKVTile;     // per-row (m, l) of both chains
   static constexpr int kOffBar = kOffX + 2 * 2 * 128 * 4;
+  // Barrier area: q | k_full[kNK] k_empty[kNK] | v_full[kNV] v_empty[kNV] |
+  // s_full[2] | o_full[2] | xs | st, then the TMEM base address and the abort flag.
+  static constexpr int kBarKF = 8, kBarKE = kBarKF + 8 * kNK, kBarVF = kBarKE + 8 * kNK;
+  static constexpr int kBarVE = kBarVF + 8 * kNV, kBarS = kBarVE + 8 * kNV, kBarO = kBarS + 16;
+  static constexpr int kBarXS = kBarO + 16, kBarST = kBarXS + 8, kSlot = kBarST + 8, kAbort = kSlot + 4;
+  static_assert(kAbort + 4 <= 256, "barrier area");
   static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
   static constexpr uint32_t kTileBytes = (uint32_t)kKVTile;
 };
@@ -273,47 +285,54 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qi = blockIdx.x / p.nsplit, sp = blockIdx.x % p.nsplit;
-  const int bl = blockIdx.y / p.H, h = blockIdx.y % p.H;
+  const int64_t cta = blockIdx.x;
+  int64_t tile = cta, piece = 0;
+  int sp = 0, ns = 1;
+  if (cta >= p.n_whole) {
+    piece = cta - p.n_whole;
+    tile = p.n_whole + piece / p.nsplit;
+    sp = (int)(piece % p.nsplit);
+    ns = p.nsplit;
+  }
+  const int qi = (int)(tile % p.nq);
+  const int bl = (int)(tile / p.nq) / p.H, h = (int)(tile / p.nq) % p.H;
   const int b = p.b0 + bl;
   const int mi = p.per_batch ? bl : 0;
   const int wc = p.per_batch ? h : b * p.H + h;
 
-  // Barriers: q | k_full[2] k_empty[2] | v_full[2] v_empty[2] | s_full[2] | o_full[2] | xs | st
   const uint32_t bar0 = sb + L::kOffBar;
   const uint32_t bar_q = bar0;
-  auto bar_kf = [&](int s) { return bar0 + 8 + 8 * s; };
-  auto bar_ke = [&](int s) { return bar0 + 24 + 8 * s; };
-  auto bar_vf = [&](int s) { return bar0 + 40 + 8 * s; };
-  auto bar_ve = [&](int s) { return bar0 + 56 + 8 * s; };
-  auto bar_s = [&](int c) { return bar0 + 72 + 8 * c; };
-  auto bar_o = [&](int c) { return bar0 + 88 + 8 * c; };
-  const uint32_t bar_xs = bar0 + 104, bar_st = bar0 + 112;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffBar + 160);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffBar + 164);
+  auto bar_kf = [&](int s) { return bar0 + L::kBarKF + 8 * s; };
+  auto bar_ke = [&](int s) { return bar0 + L::kBarKE + 8 * s; };
+  auto bar_vf = [&](int s) { return bar0 + L::kBarVF + 8 * s; };
+  auto bar_ve = [&](int s) { return bar0 + L::kBarVE + 8 * s; };
+  auto bar_s = [&](int c) { return bar0 + L::kBarS + 8 * c; };
+  auto bar_o = [&](int c) { return bar0 + L::kBarO + 8 * c; };
+  const uint32_t bar_xs = bar0 + L::kBarXS, bar_st = bar0 + L::kBarST;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffBar + L::kSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffBar + L::kAbort);
   float* xm = reinterpret_cast<float*>(smem + L::kOffX);   // [2 chains][128] row max
   float* xl = xm + 2 * 128;                                 // [2 chains][128] row sum
 
   const int S_raw = p.cnt[b * p.c_b + h * p.c_h + (int64_t)qi * p.c_q];
   const int S_all = S_raw < 0 ? 0 : (S_raw > p.smax ? p.smax : S_raw);
   if (S_all != S_raw && threadIdx.x == 0 && sp == 0 && p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
-  const int j_lo = (int)(((int64_t)S_all * sp) / p.nsplit), j_hi = (int)(((int64_t)S_all * (sp + 1)) / p.nsplit);
+  const int j_lo = (int)(((int64_t)S_all * sp) / ns), j_hi = (int)(((int64_t)S_all * (sp + 1)) / ns);
   const int S = j_hi - j_lo;  // this CTA's share of the list
   const int32_t* irow = p.idx + b * p.i_b + h * p.i_h + (int64_t)qi * p.i_q + (int64_t)j_lo * p.i_s;
-  const bool partial = p.nsplit > 1;
+  const bool partial = ns > 1;
   const int n_chain[2] = {(S + 1) / 2, S / 2};  // blocks of chain 0 (even j) and chain 1 (odd j)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar_kf(s), 1); mbar_init(bar_ke(s), 1); mbar_init(bar_vf(s), 1); mbar_init(bar_ve(s), 1);
-      mbar_init(bar_s(s), 1); mbar_init(bar_o(s), 1);
-    }
+    for (int s = 0; s < L::kNK; ++s) { mbar_init(bar_kf(s), 1); mbar_init(bar_ke(s), 1); }
+    for (int s = 0; s < L::kNV; ++s) { mbar_init(bar_vf(s), 1); mbar_init(bar_ve(s), 1); }
+    for (int c = 0; c < 2; ++c) { mbar_init(bar_s(c), 1); mbar_init(bar_o(c), 1); }
     mbar_init(bar_xs, 8); mbar_init(bar_st, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kWarpMMA0) tmem_alloc(smem_u32(smem + L::kOffBar + 160), kTmemCols);
+  if (warp == kWarpMMA0) tmem_alloc(smem_u32(smem + L::kOffBar + L::kSlot), kTmemCols);
   if (BS < 128 && warp < 4) {
     // Query rows past the block are zero so the padded MMA rows stay finite.
     for (int hf = 0; hf < L::kHalves; ++hf) {
@@ -528,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const bool store = ok && !*abort_flag;
     if (partial) {
       // Unnormalised partial of this split: O = a0 O_0 + a1 O_1 relative to mm.
-      const int64_t unit = ((int64_t)(b * p.H + h) * p.nq + qi) * p.nsplit + sp;
+      const int64_t unit = piece;
       float* po = p.part + unit * 128 * D + (int64_t)row * D;
       constexpr int kOCols = D / 2;
       const uint32_t o0 = tmem + lane_base + kColO, o1 = tmem + lane_base + kColO + 128;
@@ -615,8 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
 
 // ------------------------- split-KV combine kernel -------------------------
-// One CTA per (query block, b*h), one thread per tile row: merges the nsplit
-// partials O_s (unnormalised, reference max m_s, row sum l_s):
+// One CTA per split tile (tile n_whole + blockIdx.x of the launch), one thread
+// per tile row: merges its nsplit partials O_s (unnormalised, reference max
+// m_s, row sum l_s):
 //   M = max m_s,  w_s = 2^(m_s - M),  O = sum w_s O_s / sum w_s l_s,
 // and stores the row at its raster (or tiled) position in o.
 struct CombineArgs {
@@ -626,14 +646,17 @@ struct CombineArgs {
   int64_t o_b, o_h, o_l;
   float* lse;
   int64_t lse_len;
-  int32_t H, nq, nsplit, D, bs, f16;
+  int64_t n_whole;
+  int32_t H, b0, nq, nsplit, D, bs, f16;
   int32_t q_raster, T, LH, LW, tt, th, tw, nh, nw;
   int64_t q_len;  // tiled form: valid query rows
 };
 
 __global__ void __launch_bounds__(128) attn_combine_kernel(const CombineArgs a) {
-  const int qi = blockIdx.x, bh = blockIdx.y, row = threadIdx.x;
-  const int b = bh / a.H, h = bh % a.H;
+  const int64_t tile = a.n_whole + blockIdx.x;
+  const int qi = (int)(tile % a.nq), row = threadIdx.x;
+  const int b = a.b0 + (int)(tile / a.nq) / a.H, h = (int)(tile / a.nq) % a.H;
+  const int bh = b * a.H + h;
   if (row >= a.bs) return;
   int64_t tok;
   if (a.q_raster) {
@@ -645,7 +668,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const CombineArgs a) 
     tok = (int64_t)qi * a.bs + row;
     if (tok >= a.q_len) tok = -1;
   }
-  const int64_t unit0 = ((int64_t)bh * a.nq + qi) * a.nsplit;
+  const int64_t unit0 = (int64_t)blockIdx.x * a.nsplit;
   const float* pm = a.part + a.part_units * 128 * a.D;
   const float* pl = pm + a.part_units * 128;
   float M = -INFINITY;
@@ -780,26 +803,53 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-// Number of list splits per query block. With one CTA per SM, a launch of
-// `tiles` CTAs keeps tiles / (waves * SMs) of the machine busy; when that is
-// under 85%, split each list into the fewest parts that reach 90% (a split
-// costs a second prologue per CTA and the combine pass).
-int split_plan(int64_t tiles, int64_t smax) {
+// Tail split of one launch. At one CTA per SM, `tiles` equal query tiles run
+// as W = tiles / SMs full waves and a last wave of r = tiles % SMs tiles that
+// leaves the other SMs idle for a whole tile's time. Each of those r tiles is
+// cut into s list pieces instead (fp32 partials merged by the combine kernel).
+// s minimises the estimated finish time, in block iterations of a list of
+// `smax` blocks:  W (S + 2) + ceil(r s / SMs) (S / s + 8) + 10  (a piece pays a
+// prologue and a partial store; the combine pass runs after the launch), and
+// is used only when that beats the unsplit (W + 1) (S + 2) by 3%.
+struct TailPlan {
+  int64_t n_whole;  // tiles run whole (the first n_whole of the launch)
+  int32_t pieces;   // pieces per remaining tile (1: no split)
+};
+
+TailPlan tail_plan(int64_t tiles, int64_t smax) {
+  TailPlan tp{tiles, 1};
   const int64_t sms = sm_count();
-  auto eff = [&](int64_t units) { return (double)units / (double)(((units + sms - 1) / sms) * sms); };
-  if (tiles <= 0 || eff(tiles) >= 0.85) return 1;
-  int best = 1;
-  double best_eff = eff(tiles);
-  for (int ns = 2; ns <= 8; ++ns) {
-    if (smax / ns < 8) break;
-    const double e = eff(tiles * ns);
-    if (e > best_eff) { best = ns; best_eff = e; }
-    if (e >= 0.90) break;
+  if (tiles <= 0 || smax < 8) return tp;
+  const int64_t W = tiles / sms, r = tiles % sms;
+  if (r == 0) return tp;
+  const double S = (double)smax;
+  const double whole = (double)(W + 1) * (S + 2.0);
+  double best = whole;
+  int best_s = 1;
+  for (int s = 2; s <= 16 && S / s >= 4.0; ++s) {
+    const double waves = (double)((r * s + sms - 1) / sms);
+    const double c = (double)W * (S + 2.0) + waves * (S / s + 8.0) + 10.0;
+    if (c < best) { best = c; best_s = s; }
   }
-  return best;
+  if (best_s > 1 && best < 0.97 * whole) { tp.n_whole = tiles - r; tp.pieces = best_s; }
+  return tp;
 }
 
+// Partial slots of a plan: (tiles - n_whole) * pieces.
+int64_t plan_units(int64_t tiles, const TailPlan& tp) { return tp.pieces > 1 ? (tiles - tp.n_whole) * tp.pieces : 0; }
+
 int64_t workspace_bytes(int64_t units, int64_t D) { return units * 128 * (D + 2) * 4; }
+
+// Partial slots a call may need: one launch covers all B batches or, when the
+// operands' batch and head strides do not merge, at most kMaxMaps of them.
+int64_t call_units(int64_t B, int64_t H, int64_t nq, int64_t smax) {
+  int64_t u = 0;
+  for (int64_t nb : {B, std::min<int64_t>(B, kMaxMaps), B % kMaxMaps}) {
+    const int64_t t = nb * H * nq;
+    u = std::max(u, plan_units(t, tail_plan(t, smax)));
+  }
+  return u;
+}
 
 template <int D, int BS, bool F16>
 li_status launch_t(const Params& prm, dim3 grid, cudaStream_t stream) {
@@ -899,17 +949,8 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
   prm.ntxt = ntxt; prm.n_kv = (int)n_kv; prm.nq = (int)nq;
   if (idx->shape[3] < 0 || idx->shape[3] > (1ll << 30)) return fail(LI_ERR_SHAPE, "bad index-row width");
   prm.smax = (int)idx->shape[3];
-  prm.nsplit = 1;
-  {
-    const int ns = split_plan(B * H * nq, idx->shape[3]);
-    const int64_t units = B * H * nq * ns;
-    if (ns > 1 && workspace && workspace_bytes_avail >= workspace_bytes(units, D) && aligned16(workspace)) {
-      prm.nsplit = ns;
-      prm.part = static_cast<float*>(workspace);
-      prm.part_units = units;
-    }
-  }
   if (nq == 0 || B * H == 0) return LI_OK;
+  if (B * H * nq > INT32_MAX) return fail(LI_ERR_SHAPE, "too many query tiles for one launch");
 
   // All operands share one (b, h) addressing plan; fall back to per-batch
   // maps when any operand's batch and head strides do not merge.
@@ -949,25 +990,35 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
       }
       if (st) return st;
     }
-    dim3 grid((unsigned)(nq * prm.nsplit), (unsigned)(nb * H));
-    if (nb * H > 65535) return fail(LI_ERR_SHAPE, "B*H too large for one launch");
+    // Tail split of this launch's tiles, when the workspace holds its partials
+    // (launches run in stream order, so every launch reuses the workspace).
+    const int64_t tiles = nb * H * nq;
+    TailPlan tp = tail_plan(tiles, prm.smax);
+    const int64_t units = plan_units(tiles, tp);
+    if (tp.pieces > 1 && !(workspace && workspace_bytes_avail >= workspace_bytes(units, D) && aligned16(workspace)))
+      tp = TailPlan{tiles, 1};
+    prm.n_whole = tp.n_whole;
+    prm.nsplit = tp.pieces;
+    prm.part = tp.pieces > 1 ? static_cast<float*>(workspace) : nullptr;
+    prm.part_units = tp.pieces > 1 ? units : 0;
+    dim3 grid((unsigned)(tp.n_whole + prm.part_units));
     if (li_status st = launch((int)D, bs, f16, prm, grid, static_cast<cudaStream_t>(stream))) return st;
-  }
-  if (prm.nsplit > 1) {
-    CombineArgs ca;
-    memset(&ca, 0, sizeof(ca));
-    ca.part = prm.part; ca.part_units = prm.part_units;
-    ca.o = static_cast<uint8_t*>(o->data); ca.o_b = o->stride[0]; ca.o_h = o->stride[1]; ca.o_l = o->stride[2];
-    ca.lse = lse; ca.lse_len = nq * bs;
-    ca.H = (int)H; ca.nq = (int)nq; ca.nsplit = prm.nsplit; ca.D = (int)D; ca.bs = bs; ca.f16 = f16;
-    ca.q_raster = q_raster;
-    if (q_raster) {
-      ca.T = gq->T; ca.LH = gq->LH; ca.LW = gq->LW; ca.tt = gq->tt; ca.th = gq->th; ca.tw = gq->tw;
-      ca.nh = prm.q_nh; ca.nw = prm.q_nw;
+    if (tp.pieces > 1) {
+      CombineArgs ca;
+      memset(&ca, 0, sizeof(ca));
+      ca.part = prm.part; ca.part_units = prm.part_units; ca.n_whole = tp.n_whole;
+      ca.o = static_cast<uint8_t*>(o->data); ca.o_b = o->stride[0]; ca.o_h = o->stride[1]; ca.o_l = o->stride[2];
+      ca.lse = lse; ca.lse_len = nq * bs;
+      ca.H = (int)H; ca.b0 = (int)b0; ca.nq = (int)nq; ca.nsplit = tp.pieces; ca.D = (int)D; ca.bs = bs; ca.f16 = f16;
+      ca.q_raster = q_raster;
+      if (q_raster) {
+        ca.T = gq->T; ca.LH = gq->LH; ca.LW = gq->LW; ca.tt = gq->tt; ca.th = gq->th; ca.tw = gq->tw;
+        ca.nh = prm.q_nh; ca.nw = prm.q_nw;
+      }
+      ca.q_len = q->shape[2];
+      attn_combine_kernel<<<dim3((unsigned)(tiles - tp.n_whole)), 128, 0, static_cast<cudaStream_t>(stream)>>>(ca);
+      if (li_status st = launched("attention combine launch")) return st;
     }
-    ca.q_len = q->shape[2];
-    attn_combine_kernel<<<dim3((unsigned)nq, (unsigned)(B * H)), 128, 0, static_cast<cudaStream_t>(stream)>>>(ca);
-    if (li_status st = launched("attention combine launch")) return st;
   }
   return LI_OK;
 }
@@ -980,8 +1031,7 @@ using namespace li;
 extern "C" li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks,
                                                     int64_t max_blocks_per_row, int32_t head_dim, int64_t* bytes) {
   if (!bytes) return fail(LI_ERR_INVALID_ARG, "bytes is required");
-  const int ns = attn::split_plan(batch * heads * n_q_blocks, max_blocks_per_row);
-  *bytes = ns > 1 ? attn::workspace_bytes(batch * heads * n_q_blocks * ns, head_dim) : 0;
+  *bytes = attn::workspace_bytes(attn::call_units(batch, heads, n_q_blocks, max_blocks_per_row), head_dim);
   return LI_OK;
 }
 

@@ -84,12 +84,18 @@ def test_entry_points_validate_before_launch(lib):
 
 
 def test_split_plan_workspace(lib):
-    """Split-KV engages only when a launch leaves most of the last wave idle."""
+    """Tail split: only the tiles of a mostly idle last wave (148 SMs, one CTA
+    each) are cut into list pieces; the workspace holds exactly their partials."""
     nbytes = ctypes.c_int64()
+    unit = 128 * 130 * 4   # one fp32 partial tile of D=128: O, row max, row sum
     assert lib.li_sparse_attn_workspace_bytes(1, 24, 56, 238, 128, ctypes.byref(nbytes)) == 0
-    assert nbytes.value == 0                     # 1344 query blocks: ~9 full waves on 148 SMs
+    assert nbytes.value == 12 * 12 * unit        # 1344 tiles = 9 waves + 12: each of the 12 in 12 pieces
     assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 238, 128, ctypes.byref(nbytes)) == 0
-    assert nbytes.value > 0 and nbytes.value % (128 * 130 * 4) == 0   # 168 query blocks: split
+    assert nbytes.value == 20 * 7 * unit         # 168 tiles = 1 wave + 20: 7 pieces each
+    assert lib.li_sparse_attn_workspace_bytes(1, 16, 64, 256, 128, ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 0                     # 1024 tiles = 6 waves + 136: last wave nearly full
+    assert lib.li_sparse_attn_workspace_bytes(1, 148, 1, 100, 128, ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 0                     # whole waves
     assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 8, 128, ctypes.byref(nbytes)) == 0
     assert nbytes.value == 0                     # too few blocks per row to split
 

@@ -256,3 +256,29 @@ def test_split_kv_raster_few_heads(cuda_ok):
     torch.cuda.synchronize()
     ref, _ = O.run_sparse_attention_mg(q, k, v, 0, (LH, LW), params, "bf16", q_offset=nk - nq)
     assert_close_bf16(to_np(out), ref)
+
+
+def test_split_kv_per_batch_launches(cuda_ok):
+    """q, k, v as [B, L, H, D] storage seen as [B, H, L, D]: batch and head
+    strides do not merge, so the batches run as launches of at most four, each
+    with its own tail split and combine pass (the second at batch offset 4)."""
+    B, H, D, bs, nq, nkb, S = 5, 2, 128, 128, 3, 48, 40
+    def bhld(seed, L):
+        a, _ = rand((B, L, H, D), seed, "bf16")
+        t = torch.from_numpy(a).to(dev()).to(torch.bfloat16).transpose(1, 2)
+        return np.ascontiguousarray(a.transpose(0, 2, 1, 3)), t
+    q, tq = bhld(921, nq * bs)
+    k, tk = bhld(922, nkb * bs)
+    v, tv = bhld(923, nkb * bs)
+    assert not tq.is_contiguous()
+    idx, cnt = _random_lists(np.random.default_rng(5), B, H, nq, nkb, S)
+    out, lse = K.sparse_attn_tiled(tq, tk, tv, torch.from_numpy(idx).to(dev()), torch.from_numpy(cnt).to(dev()),
+                                   bs, return_lse=True)
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    ref, ref_lse = O.sparse_attention_tiled(q.reshape(B, H, nq, bs, D), k.reshape(B, H, nkb, bs, D),
+                                            v.reshape(B, H, nkb, bs, D), idx, cnt, p_dtype="bf16")
+    assert_close_bf16(to_np(out), ref.reshape(B, H, nq * bs, D))
+    got_lse = to_np(lse)
+    fin = np.isfinite(ref_lse.reshape(B, H, -1))
+    np.testing.assert_allclose(got_lse[fin], ref_lse.reshape(B, H, -1)[fin], atol=2e-3, rtol=1e-4)
