@@ -16,7 +16,7 @@ namespace {
 
 constexpr int kMaxD = 256;
 constexpr int kUnroll = 8;       // 16-byte copies in flight per thread (gather)
-constexpr int kPoolUnroll = 8;   // rows in flight per thread (pool / tile)
+constexpr int kPoolUnroll = 4;   // rows in flight per thread (pool / tile); 4 keeps 8 CTAs of 128 threads resident
 
 struct TileArgs {
   const uint8_t* src[2];
@@ -66,6 +66,9 @@ __device__ __forceinline__ int64_t token_of(const TileArgs& a, int blk, int r, b
 
 constexpr int kMaxBS = 1024;
 
+// DT is the element type (LI_DTYPE_*), fixed at compile time so the per-element
+// widening carries no dtype branches.
+template <int DT>
 __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   double* partial = reinterpret_cast<double*>(smem);                // [8][D]
@@ -77,8 +80,8 @@ __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
   const int s = threadIdx.x / per_stream;
   const int t2 = threadIdx.x % per_stream;
   const int g = t2 / a.CH, c = t2 % a.CH;
-  const int es = a.dtype == LI_DTYPE_FP32 ? 4 : 2;
-  const int epc = 16 / es;
+  constexpr int es = DT == LI_DTYPE_FP32 ? 4 : 2;
+  constexpr int epc = 16 / es;
   const bool pooling = (s == 0) && (a.pool != nullptr);
 
   bool any_bad = false;
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
         if (pooling) {
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (e < epc) acc[e] += (double)chunk_elem(v[u], e, a.dtype);
+            if (e < epc) acc[e] += (double)chunk_elem(v[u], e, DT);
         }
       }
     }
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
 #pragma unroll
       for (int gg = 1; gg < 8; ++gg) tot = tot + partial[gg * a.D + col];
       const float mean = __fdiv_rn(__double2float_rn(tot), (float)a.bs);
-      store_dt(pp, col, round_dt(mean, a.dtype), a.dtype);
+      store_dt(pp, col, round_dt(mean, DT), DT);
     }
   }
 }
@@ -243,7 +246,10 @@ li_status launch_tile(TileArgs& a, int64_t nblk, int64_t B, int64_t H, void* str
   dim3 grid((unsigned)nblk, (unsigned)(B * H));
   dim3 block(8 * a.CH * a.nstreams);
   const size_t smem = (size_t)8 * a.D * 8 + (size_t)a.bs * 4;
-  tile_pool_kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a.dtype == LI_DTYPE_BF16) tile_pool_kernel<LI_DTYPE_BF16><<<grid, block, smem, st>>>(a);
+  else if (a.dtype == LI_DTYPE_FP16) tile_pool_kernel<LI_DTYPE_FP16><<<grid, block, smem, st>>>(a);
+  else tile_pool_kernel<LI_DTYPE_FP32><<<grid, block, smem, st>>>(a);
   return launched("tile_pool_kernel launch");
 }
 

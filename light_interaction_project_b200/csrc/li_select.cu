@@ -381,29 +381,82 @@ using namespace li;
 namespace li {
 namespace {
 // Row-wise F.normalize of pooled rows, exactly as the selection kernel does it
-// for 'cosine': 64 rows per CTA staged as doubles, one thread per row.
-__global__ void __launch_bounds__(64) normalize_kernel(const uint8_t* x, int64_t x_b, int64_t x_h, int64_t x_n,
-                                                        uint8_t* y, int64_t y_b, int64_t y_h, int64_t y_n, int H,
-                                                        int N, int D, int dtype, float eps) {
+// for 'cosine'. 64 rows per CTA are staged as doubles. The four interleaved
+// fp64 partial sums of squares of a row go to four adjacent lanes and are
+// combined in order ((p0 + p1) + p2) + p3 through shuffles; then all 256
+// threads divide and store 16-byte chunks. DT is the element type.
+constexpr int kNormRows = 64, kNormThreads = 256;
+template <int DT>
+__global__ void __launch_bounds__(kNormThreads) normalize_kernel(const uint8_t* x, int64_t x_b, int64_t x_h,
+                                                                  int64_t x_n, uint8_t* y, int64_t y_b, int64_t y_h,
+                                                                  int64_t y_n, int H, int N, int D, float eps) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int pitch = D + 1;
-  double* rows = reinterpret_cast<double*>(smem);   // [64][pitch]
+  double* rows = reinterpret_cast<double*>(smem);                       // [64][pitch]
+  float* den = reinterpret_cast<float*>(rows + kNormRows * pitch);      // [64]
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int n0 = blockIdx.x * 64;
-  const int es = dtype == LI_DTYPE_FP32 ? 4 : 2, epc = 16 / es, CH = D / epc;
-  for (int i = threadIdx.x; i < 64 * CH; i += 64) {
+  const int n0 = blockIdx.x * kNormRows;
+  constexpr int es = DT == LI_DTYPE_FP32 ? 4 : 2, epc = 16 / es;
+  const int CH = D / epc;
+  for (int i = threadIdx.x; i < kNormRows * CH; i += kNormThreads) {
     const int r = i / CH, c = i % CH;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (n0 + r < N) v = __ldg(reinterpret_cast<const uint4*>(x + (b * x_b + h * x_h + (int64_t)(n0 + r) * x_n) * es) + c);
-    widen_chunk(v, dtype, rows + r * pitch + c * epc);
+    widen_chunk(v, DT, rows + r * pitch + c * epc);
   }
   __syncthreads();
-  if (n0 + (int)threadIdx.x < N) normalize_row(rows + threadIdx.x * pitch, D, dtype, eps);
-  __syncthreads();
-  for (int i = threadIdx.x; i < 64 * D; i += 64) {
-    const int r = i / D, d = i % D;
-    if (n0 + r < N) store_dt(y + (b * y_b + h * y_h + (int64_t)(n0 + r) * y_n) * es, d, (float)rows[r * pitch + d], dtype);
+  {
+    const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
+    const double* xr = rows + r * pitch;
+    double acc = 0.0;
+    for (int d = part; d < D; d += 4) acc = fma(xr[d], xr[d], acc);
+    const double p1 = __shfl_down_sync(0xFFFFFFFFu, acc, 1);
+    const double p2 = __shfl_down_sync(0xFFFFFFFFu, acc, 2);
+    const double p3 = __shfl_down_sync(0xFFFFFFFFu, acc, 3);
+    if (part == 0) den[r] = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(((acc + p1) + p2) + p3)), DT), eps);
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kNormRows * CH; i += kNormThreads) {
+    const int r = i / CH, c = i % CH;
+    if (n0 + r >= N) continue;
+    const double* xr = rows + r * pitch + c * epc;
+    const float dn = den[r];
+    float q[epc];
+#pragma unroll
+    for (int e = 0; e < epc; ++e) q[e] = round_dt(__fdiv_rn((float)xr[e], dn), DT);
+    uint4 out;
+    if constexpr (DT == LI_DTYPE_FP32) {
+      out = make_uint4(__float_as_uint(q[0]), __float_as_uint(q[1]), __float_as_uint(q[2]), __float_as_uint(q[3]));
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t lo = DT == LI_DTYPE_BF16 ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(q[2 * e]))
+                                                : (uint32_t)__half_as_ushort(__float2half_rn(q[2 * e]));
+        const uint32_t hi = DT == LI_DTYPE_BF16 ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(q[2 * e + 1]))
+                                                : (uint32_t)__half_as_ushort(__float2half_rn(q[2 * e + 1]));
+        w[e] = lo | (hi << 16);
+      }
+      out = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    reinterpret_cast<uint4*>(y + (b * y_b + h * y_h + (int64_t)(n0 + r) * y_n) * es)[c] = out;
+  }
+}
+
+template <int DT>
+li_status launch_normalize(const li_view4* x, li_view4* y, int64_t B, int64_t H, int64_t N, int64_t D, float eps,
+                           cudaStream_t stream) {
+  const size_t smem = (size_t)kNormRows * (D + 1) * 8 + kNormRows * 4;
+  static std::atomic<uint64_t> configured{0};
+  if (li_status st = once_per_device(configured, [] {
+        return cuda_status(cudaFuncSetAttribute(normalize_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)(kNormRows * (kMaxD + 1) * 8 + kNormRows * 4)),
+                           "normalize smem attribute");
+      })) return st;
+  normalize_kernel<DT><<<dim3((unsigned)ceil_div(N, kNormRows), (unsigned)(B * H)), kNormThreads, smem, stream>>>(
+      static_cast<const uint8_t*>(x->data), x->stride[0], x->stride[1], x->stride[2], static_cast<uint8_t*>(y->data),
+      y->stride[0], y->stride[1], y->stride[2], (int)H, (int)N, (int)D, eps);
+  return launched("normalize_kernel launch");
 }
 }  // namespace
 }  // namespace li
@@ -422,16 +475,10 @@ extern "C" li_status li_normalize_rows(const li_view4* x, li_view4* y, void* str
   const float eps = dt == LI_DTYPE_FP32 ? 1e-12f
                   : dt == LI_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(1e-12f))
                                         : __half2float(__float2half_rn(1e-12f));
-  const size_t smem = (size_t)64 * (D + 1) * 8;
-  static std::atomic<uint64_t> configured{0};
-  if (li_status st = once_per_device(configured, [] {
-        return cuda_status(cudaFuncSetAttribute(normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                (int)(64 * (kMaxD + 1) * 8)), "normalize smem attribute");
-      })) return st;
-  normalize_kernel<<<dim3((unsigned)ceil_div(N, 64), (unsigned)(B * H)), 64, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(x->data), x->stride[0], x->stride[1], x->stride[2], static_cast<uint8_t*>(y->data),
-      y->stride[0], y->stride[1], y->stride[2], (int)H, (int)N, (int)D, dt, eps);
-  return launched("normalize_kernel launch");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dt == LI_DTYPE_BF16) return launch_normalize<LI_DTYPE_BF16>(x, y, B, H, N, D, eps, st);
+  if (dt == LI_DTYPE_FP16) return launch_normalize<LI_DTYPE_FP16>(x, y, B, H, N, D, eps, st);
+  return launch_normalize<LI_DTYPE_FP32>(x, y, B, H, N, D, eps, st);
 }
 
 extern "C" li_status li_select_budget(const li_select_params* p, int64_t n_q_blocks, int64_t n_k_blocks,
