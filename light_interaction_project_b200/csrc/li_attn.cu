@@ -634,11 +634,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
 
 // ------------------------- split-KV combine kernel -------------------------
-// One CTA per split tile (tile n_whole + blockIdx.x of the launch), one thread
-// per tile row: merges its nsplit partials O_s (unnormalised, reference max
-// m_s, row sum l_s):
+// Merges the nsplit partials O_s (unnormalised, reference max m_s, row sum l_s)
+// of each split tile (tile n_whole + blockIdx.x of the launch):
 //   M = max m_s,  w_s = 2^(m_s - M),  O = sum w_s O_s / sum w_s l_s,
-// and stores the row at its raster (or tiled) position in o.
+// and stores each row at its raster (or tiled) position in o. A CTA takes
+// kCombRows rows: their per-piece weights go to shared memory first, then
+// each thread reduces one 8-column chunk of one row, so consecutive threads
+// read consecutive 32-byte pieces of the partials.
+constexpr int kCombRows = 16, kCombThreads = 256, kMaxPieces = 16;
 struct CombineArgs {
   const float* part;
   int64_t part_units;
@@ -652,47 +655,60 @@ struct CombineArgs {
   int64_t q_len;  // tiled form: valid query rows
 };
 
-__global__ void __launch_bounds__(128) attn_combine_kernel(const CombineArgs a) {
+__global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const CombineArgs a) {
+  __shared__ float wgt[kMaxPieces][kCombRows];
+  __shared__ int64_t tok_s[kCombRows];
   const int64_t tile = a.n_whole + blockIdx.x;
-  const int qi = (int)(tile % a.nq), row = threadIdx.x;
+  const int qi = (int)(tile % a.nq);
   const int b = a.b0 + (int)(tile / a.nq) / a.H, h = (int)(tile / a.nq) % a.H;
   const int bh = b * a.H + h;
-  if (row >= a.bs) return;
-  int64_t tok;
-  if (a.q_raster) {
-    const int cw = qi % a.nw, rem = qi / a.nw, ch = rem % a.nh, ct = rem / a.nh;
-    const int ow = row % a.tw, rr = row / a.tw, oh = rr % a.th, ot = rr / a.th;
-    const int t = ct * a.tt + ot, hh = ch * a.th + oh, w = cw * a.tw + ow;
-    tok = (t < a.T && hh < a.LH && w < a.LW) ? ((int64_t)t * a.LH + hh) * a.LW + w : -1;
-  } else {
-    tok = (int64_t)qi * a.bs + row;
-    if (tok >= a.q_len) tok = -1;
-  }
+  const int r0 = blockIdx.y * kCombRows;
   const int64_t unit0 = (int64_t)blockIdx.x * a.nsplit;
   const float* pm = a.part + a.part_units * 128 * a.D;
   const float* pl = pm + a.part_units * 128;
-  float M = -INFINITY;
-  for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, pm[(unit0 + sp) * 128 + row]);
-  float L = 0.f;
-  for (int sp = 0; sp < a.nsplit; ++sp) {
-    const float l = pl[(unit0 + sp) * 128 + row];
-    if (l > 0.f) L += ex2(pm[(unit0 + sp) * 128 + row] - M) * l;
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  if (a.lse && tok >= 0 && row < a.bs)
-    a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + row] = L > 0.f ? M + __log2f(L) : -INFINITY;
-  if (tok < 0) return;
-  uint8_t* dst = a.o + (b * a.o_b + h * a.o_h + tok * a.o_l) * 2;
-  for (int d0 = 0; d0 < a.D; d0 += 8) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (threadIdx.x < kCombRows) {
+    const int row = r0 + threadIdx.x;
+    int64_t tok;
+    if (a.q_raster) {
+      const int cw = qi % a.nw, rem = qi / a.nw, ch = rem % a.nh, ct = rem / a.nh;
+      const int ow = row % a.tw, rr = row / a.tw, oh = rr % a.th, ot = rr / a.th;
+      const int t = ct * a.tt + ot, hh = ch * a.th + oh, w = cw * a.tw + ow;
+      tok = (t < a.T && hh < a.LH && w < a.LW) ? ((int64_t)t * a.LH + hh) * a.LW + w : -1;
+    } else {
+      tok = (int64_t)qi * a.bs + row;
+      if (tok >= a.q_len) tok = -1;
+    }
+    tok_s[threadIdx.x] = tok;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, pm[(unit0 + sp) * 128 + row]);
+    float L = 0.f;
     for (int sp = 0; sp < a.nsplit; ++sp) {
       const float l = pl[(unit0 + sp) * 128 + row];
-      if (!(l > 0.f)) continue;
-      const float wgt = ex2(pm[(unit0 + sp) * 128 + row] - M) * inv;
+      if (l > 0.f) L += ex2(pm[(unit0 + sp) * 128 + row] - M) * l;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    for (int sp = 0; sp < a.nsplit; ++sp) {
+      const float l = pl[(unit0 + sp) * 128 + row];
+      wgt[sp][threadIdx.x] = l > 0.f ? ex2(pm[(unit0 + sp) * 128 + row] - M) * inv : 0.f;
+    }
+    if (a.lse && tok >= 0)
+      a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + row] = L > 0.f ? M + __log2f(L) : -INFINITY;
+  }
+  __syncthreads();
+  const int cpr = a.D / 8;  // 8-column chunks per row
+  for (int i = threadIdx.x; i < kCombRows * cpr; i += kCombThreads) {
+    const int lr = i / cpr, d0 = (i % cpr) * 8;
+    const int64_t tok = tok_s[lr];
+    if (tok < 0) continue;
+    const int row = r0 + lr;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < a.nsplit; ++sp) {
+      const float w = wgt[sp][lr];
+      if (w == 0.f) continue;
       const float4* src = reinterpret_cast<const float4*>(a.part + ((unit0 + sp) * 128 + row) * a.D + d0);
       const float4 x = src[0], y = src[1];
-      acc[0] += wgt * x.x; acc[1] += wgt * x.y; acc[2] += wgt * x.z; acc[3] += wgt * x.w;
-      acc[4] += wgt * y.x; acc[5] += wgt * y.y; acc[6] += wgt * y.z; acc[7] += wgt * y.w;
+      acc[0] += w * x.x; acc[1] += w * x.y; acc[2] += w * x.z; acc[3] += w * x.w;
+      acc[4] += w * y.x; acc[5] += w * y.y; acc[6] += w * y.z; acc[7] += w * y.w;
     }
     uint4 v;
     if (a.f16) {
@@ -702,7 +718,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const CombineArgs a) 
       v.x = pack2<false>(acc[0], acc[1]); v.y = pack2<false>(acc[2], acc[3]);
       v.z = pack2<false>(acc[4], acc[5]); v.w = pack2<false>(acc[6], acc[7]);
     }
-    *reinterpret_cast<uint4*>(dst + d0 * 2) = v;
+    *reinterpret_cast<uint4*>(a.o + (b * a.o_b + h * a.o_h + tok * a.o_l) * 2 + d0 * 2) = v;
   }
 }
 
@@ -826,7 +842,7 @@ TailPlan tail_plan(int64_t tiles, int64_t smax) {
   const double whole = (double)(W + 1) * (S + 2.0);
   double best = whole;
   int best_s = 1;
-  for (int s = 2; s <= 16 && S / s >= 4.0; ++s) {
+  for (int s = 2; s <= kMaxPieces && S / s >= 4.0; ++s) {
     const double waves = (double)((r * s + sms - 1) / sms);
     const double c = (double)W * (S + 2.0) + waves * (S / s + 8.0) + 10.0;
     if (c < best) { best = c; best_s = s; }
@@ -1016,7 +1032,8 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
         ca.nh = prm.q_nh; ca.nw = prm.q_nw;
       }
       ca.q_len = q->shape[2];
-      attn_combine_kernel<<<dim3((unsigned)(tiles - tp.n_whole)), 128, 0, static_cast<cudaStream_t>(stream)>>>(ca);
+      attn_combine_kernel<<<dim3((unsigned)(tiles - tp.n_whole), (unsigned)(bs / kCombRows)), kCombThreads, 0,
+                            static_cast<cudaStream_t>(stream)>>>(ca);
       if (li_status st = launched("attention combine launch")) return st;
     }
   }

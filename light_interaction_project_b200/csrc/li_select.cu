@@ -281,6 +281,106 @@ __global__ void __launch_bounds__(128) score_kernel(const SelArgs a, uint32_t* _
   }
 }
 
+// Register-tiled scores for the dot metrics (no in-kernel normalisation): a
+// CTA of 256 threads takes 16 query rows x 128 keys; thread (rg, kh, kq) forms
+// rows 4rg..4rg+3 against keys 64kh + kq and 64kh + kq + 32, each with the four
+// interleaved fp64 partial sums of the fixed order. D is staged 32 columns at
+// a time; the next slice's global loads are in flight while the current one
+// is used.
+constexpr int kTileRows = 16, kTileKeys = 128, kTileD = 32, kTileThreads = 256;
+template <int DT>
+__global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs a, uint32_t* __restrict__ keys) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int pitch = kTileD + 1;
+  double* qs = reinterpret_cast<double*>(smem);          // [kTileRows][pitch]
+  double* ks = qs + kTileRows * pitch;                   // [kTileKeys][pitch]
+  const int bh = blockIdx.z, b = bh / a.H, h = bh % a.H;
+  const int q0 = blockIdx.x * kTileRows, j0 = blockIdx.y * kTileKeys;
+  const int nrows = min(kTileRows, a.Nq - q0), nkeys = min(kTileKeys, a.Nk - j0);
+  const int tid = threadIdx.x, warp = tid >> 5, kq = tid & 31;
+  const int rg = warp >> 1, kh = warp & 1;
+  constexpr int es = DT == LI_DTYPE_FP32 ? 4 : 2, epc = 16 / es, CHD = kTileD / epc;  // 16-byte chunks per slice row
+  constexpr int kLoads = ((kTileRows + kTileKeys) * CHD + kTileThreads - 1) / kTileThreads;
+  const uint8_t* qbase = a.qp + (b * a.q_b + h * a.q_h) * es;
+  const uint8_t* kbase = a.kp + (b * a.k_b + h * a.k_h) * es;
+  uint4 pre[kLoads];
+  auto fetch = [&](int dc) {
+#pragma unroll
+    for (int l = 0; l < kLoads; ++l) {
+      const int i = tid + l * kTileThreads;
+      const int r = i / CHD, c = i % CHD;
+      pre[l] = make_uint4(0, 0, 0, 0);
+      if (r < kTileRows) {
+        if (r < nrows) pre[l] = __ldg(reinterpret_cast<const uint4*>(qbase + ((int64_t)(q0 + r) * a.q_n + dc) * es) + c);
+      } else if (r < kTileRows + kTileKeys) {
+        const int kr = r - kTileRows;
+        if (kr < nkeys) pre[l] = __ldg(reinterpret_cast<const uint4*>(kbase + ((int64_t)(j0 + kr) * a.k_n + dc) * es) + c);
+      }
+    }
+  };
+  auto stage = [&]() {
+#pragma unroll
+    for (int l = 0; l < kLoads; ++l) {
+      const int i = tid + l * kTileThreads;
+      const int r = i / CHD, c = i % CHD;
+      if (r >= kTileRows + kTileKeys) continue;
+      double* dst = (r < kTileRows ? qs + r * pitch : ks + (r - kTileRows) * pitch) + c * epc;
+#pragma unroll
+      for (int e = 0; e < epc; ++e) dst[e] = (double)chunk_elem(pre[l], e, DT);
+    }
+  };
+  double acc[4][2][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[r][m][u] = 0.0;
+  fetch(0);
+  stage();
+  __syncthreads();
+  for (int dc = 0; dc < a.D; dc += kTileD) {
+    const bool more = dc + kTileD < a.D;
+    if (more) fetch(dc + kTileD);
+#pragma unroll 2
+    for (int d = 0; d < kTileD; d += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        double kv[2], qv[4];
+#pragma unroll
+        for (int m = 0; m < 2; ++m) kv[m] = ks[(64 * kh + kq + 32 * m) * pitch + d + u];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) qv[r] = qs[(4 * rg + r) * pitch + d + u];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int m = 0; m < 2; ++m) acc[r][m][u] = fma(qv[r], kv[m], acc[r][m][u]);
+      }
+    }
+    if (more) {
+      __syncthreads();
+      stage();
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int lr = 4 * rg + r;
+    if (lr >= nrows) break;
+    const int qi = q0 + lr;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int kr = 64 * kh + kq + 32 * m;
+      if (kr >= nkeys) continue;
+      const int j = j0 + kr;
+      const double dot = ((acc[r][m][0] + acc[r][m][1]) + acc[r][m][2]) + acc[r][m][3];
+      const float sc = finish_score(a, dot, b, h, qi, j);
+      keys[((int64_t)bh * a.Nq + qi) * a.Nk + j] = radix_key(sc, DT);
+      if (a.rank) a.rank[b * a.r_b + h * a.r_h + qi * a.r_q + (int64_t)j * a.r_k] = sc;
+    }
+  }
+}
+
 // One warp per query row: top-k of the precomputed radix keys, emitted sorted.
 __global__ void __launch_bounds__(128) topk_kernel(const SelArgs a, const uint32_t* __restrict__ keys) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -594,10 +694,20 @@ li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStrea
         return cuda_status(cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 (int)kSmemBudget), "topk_kernel smem attribute");
       })) return st;
-  const size_t smem1 = (size_t)(kScoreRows + kScoreKeys) * (a.D + 1) * 8;
-  score_kernel<<<dim3((unsigned)ceil_div(a.Nq, kScoreRows), (unsigned)ceil_div(a.Nk, kScoreKeys), (unsigned)(B * H)),
-                 128, smem1, s>>>(a, keys);
-  if (li_status st = launched("score_kernel launch")) return st;
+  if (a.metric == LI_METRIC_COSINE || a.D % kTileD) {
+    // In-kernel normalisation needs whole rows staged.
+    const size_t smem1 = (size_t)(kScoreRows + kScoreKeys) * (a.D + 1) * 8;
+    score_kernel<<<dim3((unsigned)ceil_div(a.Nq, kScoreRows), (unsigned)ceil_div(a.Nk, kScoreKeys), (unsigned)(B * H)),
+                   128, smem1, s>>>(a, keys);
+    if (li_status st = launched("score_kernel launch")) return st;
+  } else {
+    const size_t smem1 = (size_t)(kTileRows + kTileKeys) * (kTileD + 1) * 8;
+    const dim3 grid((unsigned)ceil_div(a.Nq, kTileRows), (unsigned)ceil_div(a.Nk, kTileKeys), (unsigned)(B * H));
+    if (a.dtype == LI_DTYPE_BF16) score_tile_kernel<LI_DTYPE_BF16><<<grid, kTileThreads, smem1, s>>>(a, keys);
+    else if (a.dtype == LI_DTYPE_FP16) score_tile_kernel<LI_DTYPE_FP16><<<grid, kTileThreads, smem1, s>>>(a, keys);
+    else score_tile_kernel<LI_DTYPE_FP32><<<grid, kTileThreads, smem1, s>>>(a, keys);
+    if (li_status st = launched("score_tile_kernel launch")) return st;
+  }
   const size_t smem2 = (size_t)4 * a.Nk * 4;
   topk_kernel<<<dim3((unsigned)ceil_div(a.Nq, 4), (unsigned)(B * H)), 128, smem2, s>>>(a, keys);
   return launched("topk_kernel launch");
