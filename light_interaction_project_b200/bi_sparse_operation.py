@@ -38,7 +38,7 @@ def generate_prefill_indices(q_in, k_in, text_len, grid_thw, params, device, q_b
     return K.select_blocks(q_pool, k_pool, p)
 
 
-def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params, q_block_offset=None):
+def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params, q_block_offset=None, out=None):
     """One Matrix-Game sparse-attention forward — ``bi_sparse_operation.py:236-348``.
 
     ``k``/``v`` hold ``text_len`` text tokens followed by the visual tokens. Dense
@@ -46,17 +46,26 @@ def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params,
     ``q_block_offset`` (extension): q covers only the last query-chunk frames of
     the key sequence; the selection then equals those rows of the full
     bidirectional selection.
+    ``out`` (extension): a tensor shaped like q, any strides the attention's
+    store map can describe (D contiguous, 16-byte strides), that receives the
+    output — e.g. a ``[B, S, H, D]`` buffer seen as ``[B, H, S, D]``, so the
+    output projection reads it without a re-layout copy.
     """
     LH, LW = latent_hw
     if q.shape[2] % (LH * LW) != 0:
-        return dense_attention(q, k, v)
+        o = dense_attention(q, k, v)
+        if out is not None:
+            out.copy_(o)
+            o = out
+        return o
     prof = {} if ENABLE_SPARSE_PROFILING else None
     if prof is not None:
         start = torch.cuda.Event(enable_timing=True)
         start.record()
     out = sparse_forward(q, k[:, :, :text_len], v[:, :, :text_len], k[:, :, text_len:], v[:, :, text_len:],
                          latent_hw, sparse_params, L.SELECT_BIDIR, _DEFAULT_TILE,
-                         ratio=sparse_params.get("topk_ratio", 0.25), q_block_offset=q_block_offset, profile=prof)
+                         ratio=sparse_params.get("topk_ratio", 0.25), q_block_offset=q_block_offset, profile=prof,
+                         out=out)
     if prof is not None:
         torch.cuda.synchronize()
         t = lambda a, b: prof[a].elapsed_time(prof[b])  # noqa: E731

@@ -36,7 +36,7 @@ def latent_grids(q_len: int, k_len: int, latent_hw, tile):
 def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode: int, default_tile,
                    default_metric: str = "cosine", ratio: Optional[float] = None, min_budget: int = 7,
                    q_block_offset: Optional[int] = None, score_bias: Optional[torch.Tensor] = None,
-                   profile: Optional[dict] = None):
+                   profile: Optional[dict] = None, out: Optional[torch.Tensor] = None):
     LH, LW = latent_hw
     tile = tuple(int(x) for x in params.get("tile_size", default_tile))
     text_len = k_txt.shape[2] if k_txt is not None else 0
@@ -74,7 +74,8 @@ def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode:
     mark("index_end")
     mark("attn_start")
     out = K.sparse_attn_raster(q, L.grid3d(T_q, LH, LW, tile), k_txt, v_txt, k_vis, v_vis,
-                               L.grid3d(T_k, LH, LW, tile), idx, cnt, sm_scale=1.0 / math.sqrt(q.shape[-1]))
+                               L.grid3d(T_k, LH, LW, tile), idx, cnt, sm_scale=1.0 / math.sqrt(q.shape[-1]),
+                               out=out)
     mark("attn_end")
     return out
 

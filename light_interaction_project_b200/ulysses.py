@@ -132,6 +132,9 @@ class HeadShardedStack:
                                           device=self.device).to(dt))
         nq, nk = cfg.blocks()
         self.q_block_offset = nk - nq
+        # Identity frame list: the current chunk's K/V go into the buffer tail
+        # through the library's 16-byte row-gather kernel.
+        self.chunk_frames = torch.arange(cfg.query_frames, dtype=torch.int32, device=self.device)
         self.params = {"tile_size": tuple(cfg.tile), "topk_ratio": cfg.keep_ratio, "sim_metric": cfg.metric}
 
     def local_tokens(self):
@@ -151,12 +154,16 @@ class HeadShardedStack:
         S = full.shape[0]
         q = full[:, 0].permute(1, 2, 0, 3)                                       # [B, hl, S, D] view
         tail = self.k_buf[i].shape[2] - S
-        self.k_buf[i][:, :, tail:].copy_(full[:, 1].permute(1, 2, 0, 3))
-        self.v_buf[i][:, :, tail:].copy_(full[:, 2].permute(1, 2, 0, 3))
+        ft = cfg.frame_tokens
+        K.gather_frames(full[:, 1].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.k_buf[i][:, :, tail:])
+        K.gather_frames(full[:, 2].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.v_buf[i][:, :, tail:])
+        # The attention writes its output token-major ([B, S, H/P, D]), the order the
+        # return all-to-all / O projection reads, so no re-layout copy follows.
+        o_tok = torch.empty(B, S, self.hl, cfg.head_dim, device=x.device, dtype=x.dtype)
         if attn_events is not None:
             attn_events[0].record()
         o = mg.run_sparse_attention(q, self.k_buf[i], self.v_buf[i], 0, i, cfg.latent_hw, self.params,
-                                    q_block_offset=self.q_block_offset)
+                                    q_block_offset=self.q_block_offset, out=o_tok.permute(0, 2, 1, 3))
         if attn_events is not None:
             attn_events[1].record()
         back = head_to_seq(o, self.world, self.group)                           # [B, s, H, D]

@@ -282,3 +282,51 @@ def test_split_kv_per_batch_launches(cuda_ok):
     got_lse = to_np(lse)
     fin = np.isfinite(ref_lse.reshape(B, H, -1))
     np.testing.assert_allclose(got_lse[fin], ref_lse.reshape(B, H, -1)[fin], atol=2e-3, rtol=1e-4)
+
+
+def test_mg_out_buffer_token_major(cuda_ok):
+    """``out=`` (extension): the output lands in a caller buffer laid out [B, S, H, D]
+    and equals the returned-tensor form bit for bit."""
+    B, H, D, LH, LW = 1, 3, 128, 30, 52
+    _, tq = rand((B, H, 4 * LH * LW, D), 931, "bf16")
+    _, tk = rand((B, H, 8 * LH * LW, D), 932, "bf16")
+    _, tv = rand((B, H, 8 * LH * LW, D), 933, "bf16")
+    params = dict(tile_size=(4, 4, 8), topk_ratio=0.3, sim_metric="cosine")
+    nq, nk = 56, 112
+    want = mg.run_sparse_attention(tq, tk, tv, 0, 0, (LH, LW), params, q_block_offset=nk - nq)
+    buf = torch.full((B, 4 * LH * LW, H, D), float("nan"), device=dev(), dtype=torch.bfloat16)
+    got = mg.run_sparse_attention(tq, tk, tv, 0, 0, (LH, LW), params, q_block_offset=nk - nq,
+                                  out=buf.permute(0, 2, 1, 3))
+    torch.cuda.synchronize()
+    assert got.data_ptr() == buf.data_ptr()
+    assert torch.equal(buf.permute(0, 2, 1, 3), want)
+
+
+def test_stack_layer_matches_plain_restatement(cuda_ok):
+    """One head-sharded stack layer at N=1 (K/V written by the row-gather kernel,
+    attention output written token-major) equals the same layer written with
+    plain torch copies and the returned attention tensor."""
+    from light_interaction_project_b200.ulysses import HeadShardedStack, StackConfig
+    cfg = StackConfig(layers=2, heads=4, hidden=512, memory_frames=4)
+    stack = HeadShardedStack(cfg, 0, 1, dev())
+    x = stack.make_input()
+    k_ref = [t.clone() for t in stack.k_buf]
+    v_ref = [t.clone() for t in stack.v_buf]
+    y = stack.step(x)
+    nq, nk = cfg.blocks()
+    xr = x
+    for i in range(cfg.layers):
+        B, s, _ = xr.shape
+        qkv = (xr.reshape(B * s, cfg.hidden) @ stack.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
+        q = qkv[:, :, 0].permute(0, 2, 1, 3)
+        tail = k_ref[i].shape[2] - s
+        k_ref[i][:, :, tail:].copy_(qkv[:, :, 1].permute(0, 2, 1, 3))
+        v_ref[i][:, :, tail:].copy_(qkv[:, :, 2].permute(0, 2, 1, 3))
+        o = mg.run_sparse_attention(q, k_ref[i], v_ref[i], 0, i, cfg.latent_hw, stack.params,
+                                    q_block_offset=nk - nq)
+        out = o.permute(0, 2, 1, 3).reshape(B * s, cfg.heads * cfg.head_dim) @ stack.w_o[i]
+        xr = xr + out.view(B, s, cfg.hidden)
+    torch.cuda.synchronize()
+    for i in range(cfg.layers):
+        assert torch.equal(stack.k_buf[i], k_ref[i]) and torch.equal(stack.v_buf[i], v_ref[i])
+    assert torch.equal(y, xr)
