@@ -285,13 +285,23 @@ def _finish(vis_idx: np.ndarray, text_len: int, bs: int):
     return np.ascontiguousarray(idx), cnt
 
 
+def _with_bias(sim, score_bias, dtype):
+    """Additive score bias (harness extension, no reference counterpart): one
+    fp32 add rounded to the dtype, before the protection bias — the selection
+    kernels' ``score_bias`` input."""
+    if score_bias is None:
+        return sim
+    b = np.broadcast_to(np.asarray(score_bias, np.float32), sim.shape)
+    return round_to((sim.astype(np.float32) + b).astype(np.float32), dtype)
+
+
 def fast_generate_indices(q_pool, k_pool, text_len, grid_thw_q, grid_thw_k, params, dtype,
-                          return_scores=False):
+                          return_scores=False, score_bias=None):
     """Decode-path selection — ``ar_sparse_operation.py:223-284``."""
     tile = params["tile_size"]
     bs = tile[0] * tile[1] * tile[2]
     nk = k_pool.shape[2]
-    sim = block_scores(q_pool, k_pool, params.get("sim_metric", "cosine"), dtype)
+    sim = _with_bias(block_scores(q_pool, k_pool, params.get("sim_metric", "cosine"), dtype), score_bias, dtype)
     rank = sim.copy()
     n_prot, k = decode_budget(nk, tile, grid_thw_q, params)
     if n_prot > 0:
@@ -313,7 +323,7 @@ def _neighbor_matrix(nq, nk, grid_thw, q_offset=0):
 
 
 def generate_prefill_indices(q_pool, k_pool, text_len, grid_thw, params, dtype,
-                             q_offset=None, return_scores=False):
+                             q_offset=None, return_scores=False, score_bias=None):
     """Bidirectional selection — ``bi_sparse_operation_for_KV_cache.py:220-296``,
     ``bi_sparse_operation.py:179-234``.
 
@@ -331,7 +341,7 @@ def generate_prefill_indices(q_pool, k_pool, text_len, grid_thw, params, dtype,
         q_offset = 0
     if q_offset < 0 or q_offset + nq > nk:
         raise ValueError("query rows outside the key grid")
-    sim = block_scores(q_pool, k_pool, params.get("sim_metric", "cosine"), dtype)
+    sim = _with_bias(block_scores(q_pool, k_pool, params.get("sim_metric", "cosine"), dtype), score_bias, dtype)
     bias = round_to(np.float32(1.0) * np.float32(LARGE_BIAS), dtype)
     nb = _neighbor_matrix(nq, nk, grid_thw, q_offset)
     rank = round_to((sim + np.where(nb, bias, np.float32(0.0))).astype(np.float32), dtype)
