@@ -62,33 +62,80 @@ def _profile_traffic(kernel_tag):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region
+    runs: NVML reads every 20 ms (read-only queries), else nvidia-smi at 100 ms."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
+    def __init__(self, local_rank):
+        self.local_rank = local_rank
         self.proc = None
-        self.lines = []
+        self.stop = threading.Event()
+        self.samples = []      # (sm_mhz, max_mhz, set of reason names)
+        self.nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.local_rank).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.local_rank)
+
+    def _poll_nvml(self):
+        nv, h = self.nvml
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                active = {name for name, const in self.REASONS if bits & getattr(nv, const)}
+                self.samples.append((float(sm), float(mx), active))
+            except Exception:
+                pass
+            self.stop.wait(0.02)
 
     def __enter__(self):
         try:
+            self.nvml = self._nvml_handle()
+            self.t = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={self.local_rank}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t = threading.Thread(target=self._read_smi, daemon=True)
             self.t.start()
         except Exception:
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _read_smi(self):
+        names = [n for n, _ in self.REASONS]
+        for ln in self.proc.stdout:
+            parts = [x.strip() for x in ln.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                self.samples.append((float(parts[1]), float(parts[2]),
+                                     {n for n, v in zip(names, parts[5:9]) if v.lower().startswith("active")}))
+            except ValueError:
+                continue
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -97,25 +144,14 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mx = self.samples[-1][1]
+        sm = [x[0] for x in self.samples]
         loaded = [x for x in sm if x > 0.5 * (mx or max(sm))] or sm
+        reasons = set().union(*(x[2] for x in self.samples))
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------

@@ -38,7 +38,8 @@ def generate_prefill_indices(q_in, k_in, text_len, grid_thw, params, device, q_b
     return K.select_blocks(q_pool, k_pool, p)
 
 
-def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params, q_block_offset=None, out=None):
+def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params, q_block_offset=None, out=None,
+                         k_pool=None):
     """One Matrix-Game sparse-attention forward — ``bi_sparse_operation.py:236-348``.
 
     ``k``/``v`` hold ``text_len`` text tokens followed by the visual tokens. Dense
@@ -50,6 +51,8 @@ def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params,
     store map can describe (D contiguous, 16-byte strides), that receives the
     output — e.g. a ``[B, S, H, D]`` buffer seen as ``[B, H, S, D]``, so the
     output projection reads it without a re-layout copy.
+    ``k_pool`` (extension): a ``memory.KeyPoolCache`` refreshed by the caller for
+    this ``k``'s visual part; the key pooling is then skipped.
     """
     LH, LW = latent_hw
     if q.shape[2] % (LH * LW) != 0:
@@ -65,7 +68,7 @@ def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params,
     out = sparse_forward(q, k[:, :, :text_len], v[:, :, :text_len], k[:, :, text_len:], v[:, :, text_len:],
                          latent_hw, sparse_params, L.SELECT_BIDIR, _DEFAULT_TILE,
                          ratio=sparse_params.get("topk_ratio", 0.25), q_block_offset=q_block_offset, profile=prof,
-                         out=out)
+                         out=out, k_pool=k_pool)
     if prof is not None:
         torch.cuda.synchronize()
         t = lambda a, b: prof[a].elapsed_time(prof[b])  # noqa: E731

@@ -179,10 +179,10 @@ def select_blocks(q_pool: torch.Tensor, k_pool: torch.Tensor, p: L.SelectParams,
     return (idx, cnt, rank) if return_rank else (idx, cnt)
 
 
-def normalize_rows(x: torch.Tensor) -> torch.Tensor:
+def normalize_rows(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``F.normalize(x, dim=-1)`` of pooled rows with the selection's rounding — ``li_normalize_rows``."""
     lib = L.load()
-    y = torch.empty_like(x)
+    y = torch.empty_like(x) if out is None else out
     L.check(lib.li_normalize_rows(L.ptr(L.view4(x, "x")), L.ptr(L.view4(y, "y")), L.stream_ptr(x.device)),
             "li_normalize_rows")
     return y

@@ -36,7 +36,7 @@ def latent_grids(q_len: int, k_len: int, latent_hw, tile):
 def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode: int, default_tile,
                    default_metric: str = "cosine", ratio: Optional[float] = None, min_budget: int = 7,
                    q_block_offset: Optional[int] = None, score_bias: Optional[torch.Tensor] = None,
-                   profile: Optional[dict] = None, out: Optional[torch.Tensor] = None):
+                   profile: Optional[dict] = None, out: Optional[torch.Tensor] = None, k_pool=None):
     LH, LW = latent_hw
     tile = tuple(int(x) for x in params.get("tile_size", default_tile))
     text_len = k_txt.shape[2] if k_txt is not None else 0
@@ -55,22 +55,32 @@ def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode:
             ev.record()
             profile[name] = ev
 
+    metric = params.get("sim_metric", default_metric)
     mark("prep_start")
     q_pool = K.pool_blocks(q, T_q, LH, LW, tile)
-    k_pool = K.pool_blocks(k_vis, T_k, LH, LW, tile)
+    if k_pool is not None:
+        # memory.KeyPoolCache: the key pool was refreshed by the caller (only the
+        # block rows whose frames changed were re-pooled).
+        if k_pool.tile != tile or k_pool.raw is None or k_pool.raw.shape[2] != gk[0] * gk[1] * gk[2]:
+            raise ValueError("k_pool cache does not match this call's key grid")
+        key_pool = k_pool.selection_pool(metric)
+    else:
+        key_pool = K.pool_blocks(k_vis, T_k, LH, LW, tile)
     mark("prep_end")
-    metric = params.get("sim_metric", default_metric)
     if metric == "cosine":
         # Cosine similarity is the plain dot product of the normalised pools
         # (same rounding chain); normalising once here keeps it out of the
         # selection kernel's inner loop.
-        q_pool, k_pool, metric = K.normalize_rows(q_pool), K.normalize_rows(k_pool), "dot"
+        q_pool = K.normalize_rows(q_pool)
+        if k_pool is None:
+            key_pool = K.normalize_rows(key_pool)
+        metric = "dot"
     p = K.select_params(mode, metric, tile, gq, gk, text_len,
                         recent_protect=params.get("recent_protect", 0),
                         topk_ratio=params.get("topk_ratio", 1.0) if ratio is None else ratio,
                         min_budget=min_budget, q_block_offset=q_block_offset or 0)
     mark("index_start")
-    idx, cnt = K.select_blocks(q_pool, k_pool, p, score_bias=score_bias)
+    idx, cnt = K.select_blocks(q_pool, key_pool, p, score_bias=score_bias)
     mark("index_end")
     mark("attn_start")
     out = K.sparse_attn_raster(q, L.grid3d(T_q, LH, LW, tile), k_txt, v_txt, k_vis, v_vis,

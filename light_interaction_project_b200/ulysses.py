@@ -28,6 +28,7 @@ import torch.distributed as dist
 
 from . import bi_sparse_operation as mg
 from . import kernels as K
+from .memory import KeyPoolCache
 
 
 def seq_to_head(x: torch.Tensor, world: int, group=None) -> torch.Tensor:
@@ -135,6 +136,9 @@ class HeadShardedStack:
         # Identity frame list: the current chunk's K/V go into the buffer tail
         # through the library's 16-byte row-gather kernel.
         self.chunk_frames = torch.arange(cfg.query_frames, dtype=torch.int32, device=self.device)
+        # Pooled keys per layer: the memory frames are pooled once, each step
+        # re-pools only the current chunk's block rows.
+        self.key_pools = [KeyPoolCache(cfg.latent_hw, cfg.tile, cfg.metric) for _ in range(cfg.layers)]
         self.params = {"tile_size": tuple(cfg.tile), "topk_ratio": cfg.keep_ratio, "sim_metric": cfg.metric}
 
     def local_tokens(self):
@@ -160,10 +164,11 @@ class HeadShardedStack:
         # The attention writes its output token-major ([B, S, H/P, D]), the order the
         # return all-to-all / O projection reads, so no re-layout copy follows.
         o_tok = torch.empty(B, S, self.hl, cfg.head_dim, device=x.device, dtype=x.dtype)
+        kp = self.key_pools[i].refresh(self.k_buf[i], changed_from_frame=cfg.memory_frames)
         if attn_events is not None:
             attn_events[0].record()
         o = mg.run_sparse_attention(q, self.k_buf[i], self.v_buf[i], 0, i, cfg.latent_hw, self.params,
-                                    q_block_offset=self.q_block_offset, out=o_tok.permute(0, 2, 1, 3))
+                                    q_block_offset=self.q_block_offset, out=o_tok.permute(0, 2, 1, 3), k_pool=kp)
         if attn_events is not None:
             attn_events[1].record()
         back = head_to_seq(o, self.world, self.group)                           # [B, s, H, D]

@@ -330,3 +330,28 @@ def test_stack_layer_matches_plain_restatement(cuda_ok):
     for i in range(cfg.layers):
         assert torch.equal(stack.k_buf[i], k_ref[i]) and torch.equal(stack.v_buf[i], v_ref[i])
     assert torch.equal(y, xr)
+
+
+def test_key_pool_cache_matches_full_pooling(cuda_ok):
+    """memory.KeyPoolCache: pooling every block once and then only the changed
+    chunk's block rows gives the same selection and output as re-pooling all of K."""
+    from light_interaction_project_b200.memory import KeyPoolCache
+    B, H, D, LH, LW, Fm, Fq = 1, 3, 128, 30, 52, 8, 4
+    HW = LH * LW
+    params = dict(tile_size=(4, 4, 8), topk_ratio=0.3, sim_metric="cosine")
+    _, tq = rand((B, H, Fq * HW, D), 941, "bf16")
+    _, tk = rand((B, H, (Fm + Fq) * HW, D), 942, "bf16")
+    _, tv = rand((B, H, (Fm + Fq) * HW, D), 943, "bf16")
+    nq, nk = 56, 168
+    cache = KeyPoolCache((LH, LW), (4, 4, 8), "cosine")
+    for step in range(2):
+        if step:   # a new denoising step: only the current chunk's K/V change
+            _, tk2 = rand((B, H, Fq * HW, D), 950 + step, "bf16")
+            tk[:, :, Fm * HW:] = tk2
+        cache.refresh(tk, changed_from_frame=Fm)
+        got = mg.run_sparse_attention(tq, tk, tv, 0, 0, (LH, LW), params, q_block_offset=nk - nq, k_pool=cache)
+        want = mg.run_sparse_attention(tq, tk, tv, 0, 0, (LH, LW), params, q_block_offset=nk - nq)
+        full = K.normalize_rows(K.pool_blocks(tk, Fm + Fq, LH, LW, (4, 4, 8)))
+        torch.cuda.synchronize()
+        assert torch.equal(cache.selection_pool("cosine"), full), f"step {step}"
+        assert torch.equal(got, want), f"step {step}"
