@@ -185,17 +185,23 @@ struct GatherArgs {
   int32_t src_frames, frame_tokens, H, dtype, CH;
 };
 
-__global__ void gather_frames_kernel(const GatherArgs a) {
-  const int f = blockIdx.x;
+// One CTA per (kGatherRows-token piece of a retained frame, b*h): the frame's
+// rows are split so that even a few heads and frames fill the GPU.
+constexpr int kGatherRows = 64;
+__global__ void __launch_bounds__(256) gather_frames_kernel(const GatherArgs a) {
+  const int pieces = (a.frame_tokens + kGatherRows - 1) / kGatherRows;
+  const int f = blockIdx.x / pieces, piece = blockIdx.x % pieces;
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
   const int es = a.dtype == LI_DTYPE_FP32 ? 4 : 2;
   const int sf = a.frame_ids[f];
   const bool ok = sf >= 0 && sf < a.src_frames;
   if (!ok && threadIdx.x == 0 && a.err) atomicOr(a.err, (unsigned)LI_DEVERR_BAD_INDEX);
-  const uint8_t* src = a.src + (b * a.s_b + h * a.s_h + (int64_t)sf * a.frame_tokens * a.s_l) * es;
-  uint8_t* dst = a.dst + (b * a.d_b + h * a.d_h + (int64_t)f * a.frame_tokens * a.d_l) * es;
-  const int total = a.frame_tokens * a.CH;
+  const int r0 = piece * kGatherRows;
+  const int nrows = min(kGatherRows, a.frame_tokens - r0);
+  const uint8_t* src = a.src + (b * a.s_b + h * a.s_h + ((int64_t)sf * a.frame_tokens + r0) * a.s_l) * es;
+  uint8_t* dst = a.dst + (b * a.d_b + h * a.d_h + ((int64_t)f * a.frame_tokens + r0) * a.d_l) * es;
+  const int total = nrows * a.CH;
   for (int base = threadIdx.x; base < total; base += blockDim.x * kUnroll) {
     uint4 v[kUnroll];
 #pragma unroll
@@ -395,7 +401,9 @@ extern "C" li_status li_gather_frames(const li_view4* src, const int32_t* frame_
   a.src_frames = (int)(L / frame_tokens); a.frame_tokens = frame_tokens; a.H = (int)H;
   a.dtype = dtype; a.CH = (int)(D * dtype_size(dtype) / 16);
   if (n_frames == 0 || B * H == 0) return LI_OK;
-  gather_frames_kernel<<<dim3((unsigned)n_frames, (unsigned)(B * H)), dim3(256), 0,
+  const int64_t pieces = ceil_div(frame_tokens, kGatherRows);
+  if ((int64_t)n_frames * pieces > 2147483647 || B * H > 65535) return fail(LI_ERR_SHAPE, "grid too large");
+  gather_frames_kernel<<<dim3((unsigned)(n_frames * pieces), (unsigned)(B * H)), dim3(256), 0,
                          static_cast<cudaStream_t>(stream)>>>(a);
   return launched("gather_frames_kernel launch");
 }

@@ -382,39 +382,84 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
 }
 
 // One warp per query row: top-k of the precomputed radix keys, emitted sorted.
+// An 8-bit radix select finds the k-th largest key T (key_bits / 8 histogram
+// passes over the row, each followed by a warp scan of 256 bins); one pass in
+// ascending j then emits every key above T and the lowest-index keys equal to
+// T until k are taken — the order of the composite key
+// (radix_key << idx_bits) | (2^idx_bits - 1 - j), ties to the lowest index.
 __global__ void __launch_bounds__(128) topk_kernel(const SelArgs a, const uint32_t* __restrict__ keys) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int qi = blockIdx.x * 4 + warp, bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
   if (qi >= a.Nq) return;
-  uint32_t* rk = reinterpret_cast<uint32_t*>(smem) + warp * a.Nk;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256;
+  uint32_t* rk = reinterpret_cast<uint32_t*>(smem) + 4 * 256 + warp * a.Nk;
   const uint32_t* src = keys + ((int64_t)bh * a.Nq + qi) * a.Nk;
   for (int j = lane; j < a.Nk; j += 32) rk[j] = src[j];
   __syncwarp();
-  const uint64_t low_mask = (1ull << a.idx_bits) - 1ull;
   const int k = a.k_budget;
-  uint64_t thr = 0;
+  uint32_t T = 0;        // the k-th largest key
+  int ties = 0;          // keys equal to T that are taken
   if (k > 0 && k < a.Nk) {
-    for (int bit = a.key_bits + a.idx_bits - 1; bit >= 0; --bit) {
-      const uint64_t cand = thr | (1ull << bit);
-      int c = 0;
-      for (int j = lane; j < a.Nk; j += 32) c += (((uint64_t)rk[j] << a.idx_bits) | (low_mask - (uint64_t)j)) >= cand;
+    uint32_t prefix = 0;
+    int need = k;        // rank of the k-th largest within the keys matching `prefix`
+    for (int shift = a.key_bits - 8; shift >= 0; shift -= 8) {
+      const uint32_t hi = shift + 8 >= 32 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int d = lane; d < 256; d += 32) hist[d] = 0;
+      __syncwarp();
+      for (int j = lane; j < a.Nk; j += 32) {
+        const uint32_t key = rk[j];
+        if ((key & hi) == prefix) atomicAdd(&hist[(key >> shift) & 0xFFu], 1u);
+      }
+      __syncwarp();
+      // Lane l owns digits 255-8l .. 248-8l; counts of larger digits come first.
+      uint32_t c[8], sum = 0;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
-      if (c >= k) thr = cand;
+      for (int e = 0; e < 8; ++e) { c[e] = hist[255 - 8 * lane - e]; sum += c[e]; }
+      uint32_t before = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, before, o);
+        if (lane >= o) before += t;
+      }
+      before -= sum;     // keys with a larger digit than this lane's range
+      int found = -1, left = 0;
+      if ((int)before < need && (int)(before + sum) >= need) {
+        uint32_t run = before;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (found < 0 && (int)(run + c[e]) >= need) { found = 255 - 8 * lane - e; left = need - (int)run; }
+          run += c[e];
+        }
+      }
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, found >= 0);
+      const int src_lane = m ? __ffs(m) - 1 : 0;
+      const int digit = __shfl_sync(0xFFFFFFFFu, found, src_lane);
+      need = __shfl_sync(0xFFFFFFFFu, left, src_lane);
+      prefix |= (uint32_t)digit << shift;
+      __syncwarp();
     }
+    T = prefix;
+    ties = need;
   }
   int32_t* out = a.idx + b * a.i_b + h * a.i_h + (int64_t)qi * a.i_q;
   for (int t = lane; t < a.ntxt; t += 32) out[(int64_t)t * a.i_s] = t;
-  int pos = 0;
+  int pos = 0, eq_seen = 0;
   if (k > 0) {
     for (int base = 0; base < a.Nk; base += 32) {
       const int j = base + lane;
-      bool sel = false;
-      if (j < a.Nk) sel = (k >= a.Nk) || ((((uint64_t)rk[j] << a.idx_bits) | (low_mask - (uint64_t)j)) >= thr);
+      bool gt = false, eq = false;
+      if (j < a.Nk) {
+        const uint32_t key = rk[j];
+        gt = key > T;
+        eq = key == T;
+      }
+      const unsigned em = __ballot_sync(0xFFFFFFFFu, eq);
+      const bool sel = j < a.Nk && ((k >= a.Nk) || gt || (eq && eq_seen + __popc(em & ((1u << lane) - 1u)) < ties));
       const unsigned m = __ballot_sync(0xFFFFFFFFu, sel);
       if (sel) out[(int64_t)(a.ntxt + pos + __popc(m & ((1u << lane) - 1u))) * a.i_s] = j + a.ntxt;
       pos += __popc(m);
+      eq_seen += __popc(em);
     }
   }
   if (lane == 0) a.cnt[b * a.c_b + h * a.c_h + (int64_t)qi * a.c_q] = a.ntxt + k;
@@ -663,6 +708,9 @@ li_status prepare_select(const li_view4* q_pool, const li_view4* k_pool, const l
 
 int64_t select_ws_bytes(int64_t B, int64_t H, int64_t Nq, int64_t Nk) { return B * H * Nq * Nk * 4; }
 
+// Shared memory of topk_kernel: four warps' 256-bin histograms and key rows.
+size_t topk_smem(int64_t Nk) { return (size_t)4 * 256 * 4 + (size_t)16 * Nk; }
+
 // Single-kernel selection (no workspace).
 li_status launch_single(SelArgs& a, int64_t B, int64_t H, cudaStream_t s) {
   const int64_t D = a.D, Nk = a.Nk, Nq = a.Nq;
@@ -708,7 +756,7 @@ li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStrea
     else score_tile_kernel<LI_DTYPE_FP32><<<grid, kTileThreads, smem1, s>>>(a, keys);
     if (li_status st = launched("score_tile_kernel launch")) return st;
   }
-  const size_t smem2 = (size_t)4 * a.Nk * 4;
+  const size_t smem2 = topk_smem(a.Nk);
   topk_kernel<<<dim3((unsigned)ceil_div(a.Nq, 4), (unsigned)(B * H)), 128, smem2, s>>>(a, keys);
   return launched("topk_kernel launch");
 }
@@ -718,7 +766,7 @@ li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStrea
 extern "C" li_status li_select_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks, int64_t n_k_blocks,
                                                int64_t* bytes) {
   if (!bytes) return fail(LI_ERR_INVALID_ARG, "bytes is required");
-  *bytes = (size_t)16 * n_k_blocks <= kSmemBudget ? select_ws_bytes(batch, heads, n_q_blocks, n_k_blocks) : 0;
+  *bytes = topk_smem(n_k_blocks) <= kSmemBudget ? select_ws_bytes(batch, heads, n_q_blocks, n_k_blocks) : 0;
   return LI_OK;
 }
 
@@ -732,7 +780,7 @@ extern "C" li_status li_select_blocks(const li_view4* q_pool, const li_view4* k_
   if (B * H == 0 || a.Nq == 0) return LI_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t need = select_ws_bytes(B, H, a.Nq, a.Nk);
-  if (workspace && workspace_bytes >= need && (size_t)16 * a.Nk <= kSmemBudget && aligned16(workspace))
+  if (workspace && workspace_bytes >= need && topk_smem(a.Nk) <= kSmemBudget && aligned16(workspace))
     return launch_two(a, B, H, static_cast<uint32_t*>(workspace), s);
   return launch_single(a, B, H, s);
 }
@@ -792,7 +840,7 @@ extern "C" li_status li_select_blocks_static(const li_view4* q_pool, const li_vi
                 "bytes of scratch; the static buffer holds %lld (use li_select_blocks with a workspace)",
                 (long long)B, (long long)H, (long long)a.Nq, (long long)a.Nk, (long long)need,
                 (long long)LI_SELECT_STATIC_SCRATCH_BYTES);
-  if ((size_t)16 * a.Nk > kSmemBudget)
+  if (topk_smem(a.Nk) > kSmemBudget)
     return fail(LI_ERR_UNSUPPORTED, "%lld key blocks exceed the top-k kernel's shared memory", (long long)a.Nk);
   uint32_t* scratch = nullptr;
   if (li_status st = static_scratch(&scratch)) return st;
