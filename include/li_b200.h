@@ -114,6 +114,16 @@ li_status li_tile_pool(const li_view4* src0, const li_view4* src1, const int32_t
                        int64_t dst_block_offset, li_view4* pool, int64_t pool_block_offset,
                        void* stream);
 
+/* Pool-only form of li_tile_pool for one stream, optionally normalised: with
+ * `normalized` != 0 the stored row is F.normalize(mean, dim=-1) with the
+ * selection's rounding chain (sqrt of the fp64 sum of squares -> fp32 -> dtype,
+ * clamped at dtype(1e-12), fp32 quotient -> dtype), i.e. li_normalize_rows of
+ * the li_tile_pool mean, bit for bit, in one launch — the block mean of
+ * launch_q_prep / launch_kv_prep plus the F.normalize of the 'cosine' metric
+ * (ar_sparse_operation.py:252, bi_sparse_operation.py:197). */
+li_status li_pool_blocks(const li_view4* src, const int32_t* frame_ids, li_grid3d grid, li_view4* pool,
+                         int64_t pool_block_offset, int32_t normalized, void* stream);
+
 /* Text K/V into the first blocks of the tiled K/V buffers, zero-padded to a
  * block multiple — replaces the F.pad + copy_ at ar_sparse_operation.py:337-344
  * (bi_sparse_operation_for_KV_cache.py:369-375; bi_sparse_operation.py:279-286).

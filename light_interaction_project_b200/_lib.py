@@ -72,6 +72,7 @@ SIGNATURES = {
     "li_kernel_launches": ([], c_uint64),
     "li_tile_pool": ([POINTER(View4), POINTER(View4), c_void_p, Grid3d, POINTER(View5), POINTER(View5), c_int64,
                       POINTER(View4), c_int64, c_void_p], c_int32),
+    "li_pool_blocks": ([POINTER(View4), c_void_p, Grid3d, POINTER(View4), c_int64, c_int32, c_void_p], c_int32),
     "li_text_blocks": ([POINTER(View4), POINTER(View4), c_int32, POINTER(View5), POINTER(View5), c_void_p], c_int32),
     "li_untile": ([POINTER(View5), Grid3d, POINTER(View4), c_void_p], c_int32),
     "li_gather_frames": ([POINTER(View4), c_void_p, c_int32, c_int32, POINTER(View4), c_void_p, c_void_p], c_int32),

@@ -34,6 +34,8 @@ struct TileArgs {
   int32_t n_tokens;    // flat: valid tokens
   int32_t T, LH, LW, tt, th, tw, nh, nw;
   int32_t H, bs, D, dtype, CH;
+  int32_t normalize;   // 1: store F.normalize of the block mean instead of the mean
+  float eps;           // dtype(1e-12), the clamp of the normalisation
 };
 
 // Raster token of row r of block `blk` (-1: padding or a rejected frame id).
@@ -73,6 +75,8 @@ __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   double* partial = reinterpret_cast<double*>(smem);                // [8][D]
   int32_t* rowtok = reinterpret_cast<int32_t*>(partial + 8 * a.D);  // token of each row, -1 = zero row
+  float* prow = reinterpret_cast<float*>(rowtok + a.bs);            // [D] dtype-rounded means
+  double* nrm = reinterpret_cast<double*>(smem);                    // [4] partial sums (reuses partial)
   const int blk = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
@@ -134,15 +138,34 @@ __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
   }
   __syncthreads();
   if (pooling && g == 0) {
-    uint8_t* pp = a.pool + (b * a.p_b + h * a.p_h + (blk + a.pool_off) * a.p_n) * es;
     for (int e = 0; e < epc; ++e) {
       const int col = c * epc + e;
       double tot = partial[col];
 #pragma unroll
       for (int gg = 1; gg < 8; ++gg) tot = tot + partial[gg * a.D + col];
-      const float mean = __fdiv_rn(__double2float_rn(tot), (float)a.bs);
-      store_dt(pp, col, round_dt(mean, DT), DT);
+      prow[col] = round_dt(__fdiv_rn(__double2float_rn(tot), (float)a.bs), DT);
     }
+  }
+  __syncthreads();
+  uint8_t* pp = a.pool + (b * a.p_b + h * a.p_h + (blk + a.pool_off) * a.p_n) * es;
+  if (!a.normalize) {
+    if (pooling && g == 0)
+      for (int e = 0; e < epc; ++e) store_dt(pp, c * epc + e, prow[c * epc + e], DT);
+    return;
+  }
+  // F.normalize of the mean row: four interleaved fp64 partial sums of squares
+  // (d mod 4, ascending d) combined in order, the selection's rounding chain.
+  if (threadIdx.x < 4) {
+    double acc = 0.0;
+    for (int d = threadIdx.x; d < a.D; d += 4) acc = fma((double)prow[d], (double)prow[d], acc);
+    nrm[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (pooling && g == 0) {
+    const double sum = ((nrm[0] + nrm[1]) + nrm[2]) + nrm[3];
+    const float den = fmaxf(round_dt(__fsqrt_rn(__double2float_rn(sum)), DT), a.eps);
+    for (int e = 0; e < epc; ++e)
+      store_dt(pp, c * epc + e, round_dt(__fdiv_rn(prow[c * epc + e], den), DT), DT);
   }
 }
 
@@ -251,7 +274,7 @@ li_status launch_tile(TileArgs& a, int64_t nblk, int64_t B, int64_t H, void* str
   if (nblk > 2147483647 || B * H > 65535) return fail(LI_ERR_SHAPE, "grid too large");
   dim3 grid((unsigned)nblk, (unsigned)(B * H));
   dim3 block(8 * a.CH * a.nstreams);
-  const size_t smem = (size_t)8 * a.D * 8 + (size_t)a.bs * 4;
+  const size_t smem = (size_t)8 * a.D * 8 + (size_t)a.bs * 4 + (size_t)a.D * 4;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a.dtype == LI_DTYPE_BF16) tile_pool_kernel<LI_DTYPE_BF16><<<grid, block, smem, st>>>(a);
   else if (a.dtype == LI_DTYPE_FP16) tile_pool_kernel<LI_DTYPE_FP16><<<grid, block, smem, st>>>(a);
@@ -264,10 +287,11 @@ li_status launch_tile(TileArgs& a, int64_t nblk, int64_t B, int64_t H, void* str
 
 using namespace li;
 
-extern "C" li_status li_tile_pool(const li_view4* src0, const li_view4* src1, const int32_t* frame_ids,
-                                  li_grid3d grid, li_view5* dst0, li_view5* dst1,
-                                  int64_t dst_block_offset, li_view4* pool, int64_t pool_block_offset,
-                                  void* stream) {
+namespace li {
+namespace {
+li_status tile_pool_impl(const li_view4* src0, const li_view4* src1, const int32_t* frame_ids, li_grid3d grid,
+                         li_view5* dst0, li_view5* dst1, int64_t dst_block_offset, li_view4* pool,
+                         int64_t pool_block_offset, int normalize, void* stream) {
   if (!src0) return fail(LI_ERR_INVALID_ARG, "src0 is required");
   if ((src1 == nullptr) != (dst1 == nullptr)) return fail(LI_ERR_INVALID_ARG, "dst1 must be given iff src1 is");
   if (li_status st = check_grid(grid)) return st;
@@ -314,7 +338,28 @@ extern "C" li_status li_tile_pool(const li_view4* src0, const li_view4* src1, co
     a.p_b = pool->stride[0]; a.p_h = pool->stride[1]; a.p_n = pool->stride[2];
   }
   if (!dst0 && !pool && !dst1) return LI_OK;
+  a.normalize = normalize;
+  a.eps = dtype == LI_DTYPE_FP32 ? 1e-12f
+        : dtype == LI_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(1e-12f))
+                                 : __half2float(__float2half_rn(1e-12f));
+  if (normalize && !pool) return fail(LI_ERR_INVALID_ARG, "normalised pooling needs a pool output");
   return launch_tile(a, nblk, B, H, stream);
+}
+}  // namespace
+}  // namespace li
+
+extern "C" li_status li_tile_pool(const li_view4* src0, const li_view4* src1, const int32_t* frame_ids,
+                                  li_grid3d grid, li_view5* dst0, li_view5* dst1,
+                                  int64_t dst_block_offset, li_view4* pool, int64_t pool_block_offset,
+                                  void* stream) {
+  return tile_pool_impl(src0, src1, frame_ids, grid, dst0, dst1, dst_block_offset, pool, pool_block_offset, 0,
+                        stream);
+}
+
+extern "C" li_status li_pool_blocks(const li_view4* src, const int32_t* frame_ids, li_grid3d grid, li_view4* pool,
+                                    int64_t pool_block_offset, int32_t normalized, void* stream) {
+  return tile_pool_impl(src, nullptr, frame_ids, grid, nullptr, nullptr, 0, pool, pool_block_offset,
+                        normalized ? 1 : 0, stream);
 }
 
 extern "C" li_status li_text_blocks(const li_view4* src0, const li_view4* src1, int32_t bs,

@@ -72,12 +72,23 @@ def tile_pool(src0: torch.Tensor, grid: L.Grid3d, *, src1: Optional[torch.Tensor
                              L.ptr(pv), int(pool_block_offset), L.stream_ptr(src0.device)), "li_tile_pool")
 
 
-def pool_blocks(x: torch.Tensor, T: int, LH: int, LW: int, tile, frame_ids=None) -> torch.Tensor:
-    """Per-block mean of a raster tensor ``[B,H,L,D]`` -> ``[B,H,Nblk,D]`` (no tiled copy)."""
+def pool_blocks(x: torch.Tensor, T: int, LH: int, LW: int, tile, frame_ids=None, normalized: bool = False,
+                out: Optional[torch.Tensor] = None, block_offset: int = 0) -> torch.Tensor:
+    """Per-block mean of a raster tensor ``[B,H,L,D]`` -> ``[B,H,Nblk,D]`` (no tiled copy) —
+    ``li_pool_blocks``. ``normalized``: the rows are ``F.normalize``-d in the same launch
+    (the 'cosine' selection input). ``out``/``block_offset``: write into rows
+    ``block_offset..`` of an existing pool."""
+    lib = L.load()
     nt, nh, nw = grid_blocks(T, LH, LW, tile)
     B, H, _, D = x.shape
-    pool = torch.empty((B, H, nt * nh * nw, D), device=x.device, dtype=x.dtype)
-    tile_pool(x, L.grid3d(T, LH, LW, tile), frame_ids=frame_ids, pool=pool)
+    pool = torch.empty((B, H, nt * nh * nw, D), device=x.device, dtype=x.dtype) if out is None else out
+    fid = None
+    if frame_ids is not None:
+        if frame_ids.dtype != torch.int32 or not frame_ids.is_cuda or frame_ids.numel() < T:
+            raise ValueError("frame_ids must be a CUDA int32 tensor with one entry per logical frame")
+        fid = frame_ids.contiguous().data_ptr()
+    L.check(lib.li_pool_blocks(L.ptr(L.view4(x, "src")), fid, L.grid3d(T, LH, LW, tile), L.ptr(L.view4(pool, "pool")),
+                               int(block_offset), 1 if normalized else 0, L.stream_ptr(x.device)), "li_pool_blocks")
     return pool
 
 

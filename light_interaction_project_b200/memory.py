@@ -49,17 +49,16 @@ class KeyPoolCache:
     Within one query chunk's denoising steps the memory frames' K is constant and
     only the current chunk's frames change. :meth:`refresh` pools every key block
     on its first call and afterwards only the block rows from
-    ``changed_from_frame`` on (rounded down to a block-row boundary); for
-    ``cosine`` it keeps the normalised rows as well. The pooled rows are the same
-    bits a full re-pool gives, so selection is unchanged.
+    ``changed_from_frame`` on (rounded down to a block-row boundary). For
+    ``cosine`` the stored rows are normalised in the same launch. The rows are the
+    same bits a full re-pool gives, so selection is unchanged.
     """
 
     def __init__(self, latent_hw, tile, metric: str = "cosine"):
         self.latent_hw = tuple(latent_hw)
         self.tile = tuple(int(t) for t in tile)
         self.metric = metric
-        self.raw: Optional[torch.Tensor] = None
-        self.normed: Optional[torch.Tensor] = None
+        self.pool: Optional[torch.Tensor] = None
         self._shape = None
 
     def refresh(self, k_vis: torch.Tensor, changed_from_frame: int = 0) -> "KeyPoolCache":
@@ -69,11 +68,10 @@ class KeyPoolCache:
             raise ValueError("k_vis length must be a whole number of latent frames")
         T = k_vis.shape[2] // HW
         shape = (k_vis.shape[0], k_vis.shape[1], T, k_vis.shape[3], k_vis.dtype, k_vis.device)
-        if self.raw is None or shape != self._shape:
+        if self.pool is None or shape != self._shape:
             nt, nh, nw = K.grid_blocks(T, LH, LW, self.tile)
-            self.raw = torch.empty((k_vis.shape[0], k_vis.shape[1], nt * nh * nw, k_vis.shape[3]),
-                                   device=k_vis.device, dtype=k_vis.dtype)
-            self.normed = torch.empty_like(self.raw) if self.metric == "cosine" else None
+            self.pool = torch.empty((k_vis.shape[0], k_vis.shape[1], nt * nh * nw, k_vis.shape[3]),
+                                    device=k_vis.device, dtype=k_vis.dtype)
             self._shape = shape
             changed_from_frame = 0
         tt = self.tile[0]
@@ -81,17 +79,14 @@ class KeyPoolCache:
         if f0 >= T:
             return self
         _, nh, nw = K.grid_blocks(T, LH, LW, self.tile)
-        off = (f0 // tt) * nh * nw
-        K.tile_pool(k_vis[:, :, f0 * HW:], K.L.grid3d(T - f0, LH, LW, self.tile), pool=self.raw,
-                    pool_block_offset=off)
-        if self.normed is not None:
-            K.normalize_rows(self.raw[:, :, off:], out=self.normed[:, :, off:])
+        K.pool_blocks(k_vis[:, :, f0 * HW:], T - f0, LH, LW, self.tile, normalized=self.metric == "cosine",
+                      out=self.pool, block_offset=(f0 // tt) * nh * nw)
         return self
 
     def selection_pool(self, metric: str) -> torch.Tensor:
         """The key pool the selection reads for ``metric`` (normalised for cosine)."""
-        if self.raw is None:
+        if self.pool is None:
             raise RuntimeError("KeyPoolCache.refresh() has not been called")
         if metric != self.metric:
             raise ValueError(f"cache built for metric {self.metric!r}, selection uses {metric!r}")
-        return self.normed if metric == "cosine" else self.raw
+        return self.pool

@@ -56,24 +56,22 @@ def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode:
             profile[name] = ev
 
     metric = params.get("sim_metric", default_metric)
+    # Cosine similarity is the plain dot product of the normalised pools (same
+    # rounding chain); the pooling kernel normalises the rows it writes, which
+    # keeps the normalisation out of the selection kernel's inner loop.
+    cosine = metric == "cosine"
     mark("prep_start")
-    q_pool = K.pool_blocks(q, T_q, LH, LW, tile)
+    q_pool = K.pool_blocks(q, T_q, LH, LW, tile, normalized=cosine)
     if k_pool is not None:
         # memory.KeyPoolCache: the key pool was refreshed by the caller (only the
         # block rows whose frames changed were re-pooled).
-        if k_pool.tile != tile or k_pool.raw is None or k_pool.raw.shape[2] != gk[0] * gk[1] * gk[2]:
+        if k_pool.tile != tile or k_pool.pool is None or k_pool.pool.shape[2] != gk[0] * gk[1] * gk[2]:
             raise ValueError("k_pool cache does not match this call's key grid")
         key_pool = k_pool.selection_pool(metric)
     else:
-        key_pool = K.pool_blocks(k_vis, T_k, LH, LW, tile)
+        key_pool = K.pool_blocks(k_vis, T_k, LH, LW, tile, normalized=cosine)
     mark("prep_end")
-    if metric == "cosine":
-        # Cosine similarity is the plain dot product of the normalised pools
-        # (same rounding chain); normalising once here keeps it out of the
-        # selection kernel's inner loop.
-        q_pool = K.normalize_rows(q_pool)
-        if k_pool is None:
-            key_pool = K.normalize_rows(key_pool)
+    if cosine:
         metric = "dot"
     p = K.select_params(mode, metric, tile, gq, gk, text_len,
                         recent_protect=params.get("recent_protect", 0),

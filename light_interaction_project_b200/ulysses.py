@@ -44,6 +44,28 @@ def seq_to_head(x: torch.Tensor, world: int, group=None) -> torch.Tensor:
     return recv.reshape(world * s, N, B, hl, D)
 
 
+def rank_major_qkv_weight(w_qkv: torch.Tensor, world: int, heads: int, head_dim: int) -> torch.Tensor:
+    """``[hidden, 3*H*D]`` QKV weight (columns ``(q|k|v, head, d)``) -> ``[P, hidden, 3*(H/P)*D]``:
+    block p holds the q/k/v columns of rank p's heads, so ``x @ w`` (batched over p) is
+    already the all-to-all send buffer ``[P, s, 3, H/P, D]`` — no pack copy."""
+    hidden = w_qkv.shape[0]
+    hl = heads // world
+    return (w_qkv.view(hidden, 3, world, hl, head_dim).permute(2, 0, 1, 3, 4)
+            .reshape(world, hidden, 3 * hl * head_dim).contiguous())
+
+
+def qkv_to_head(x2d: torch.Tensor, w_rank_major: torch.Tensor, world: int, heads: int, head_dim: int,
+                group=None) -> torch.Tensor:
+    """QKV projection of this rank's ``s`` tokens (batch 1) straight into the
+    all-to-all send order, then the exchange: returns ``[P*s, 3, 1, H/P, D]``
+    (all tokens, this rank's heads), the layout :func:`seq_to_head` returns."""
+    s = x2d.shape[0]
+    send = torch.matmul(x2d, w_rank_major)                 # [P, s, 3*hl*D]
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.view(world * s, 3, 1, heads // world, head_dim)
+
+
 def head_to_seq(o: torch.Tensor, world: int, group=None) -> torch.Tensor:
     """``[B, H/P, S, D]`` (this rank's heads, all tokens) -> ``[B, S/P, H, D]``."""
     B, hl, S, D = o.shape
@@ -123,6 +145,9 @@ class HeadShardedStack:
                       for _ in range(cfg.layers)]
         self.w_o = [(torch.randn(hd, cfg.hidden, generator=gw, device=self.device) * std).to(dt)
                     for _ in range(cfg.layers)]
+        # N > 1, batch 1: the QKV projection writes the all-to-all send buffer directly.
+        self.w_qkv_rank = ([rank_major_qkv_weight(w, world, cfg.heads, cfg.head_dim) for w in self.w_qkv]
+                           if world > 1 and cfg.batch == 1 else None)
         kv_tokens = cfg.kv_frames * cfg.frame_tokens
         self.k_buf: List[torch.Tensor] = []
         self.v_buf: List[torch.Tensor] = []
@@ -153,8 +178,12 @@ class HeadShardedStack:
     def layer(self, i: int, x: torch.Tensor, attn_events=None) -> torch.Tensor:
         cfg = self.cfg
         B, s, _ = x.shape
-        qkv = (x.reshape(B * s, cfg.hidden) @ self.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
-        full = seq_to_head(qkv.permute(2, 0, 1, 3, 4), self.world, self.group)   # [S, 3, B, hl, D]
+        if self.w_qkv_rank is not None:
+            full = qkv_to_head(x.reshape(B * s, cfg.hidden), self.w_qkv_rank[i], self.world, cfg.heads,
+                               cfg.head_dim, self.group)                         # [S, 3, B, hl, D]
+        else:
+            qkv = (x.reshape(B * s, cfg.hidden) @ self.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
+            full = seq_to_head(qkv.permute(2, 0, 1, 3, 4), self.world, self.group)   # [S, 3, B, hl, D]
         S = full.shape[0]
         q = full[:, 0].permute(1, 2, 0, 3)                                       # [B, hl, S, D] view
         tail = self.k_buf[i].shape[2] - S

@@ -127,3 +127,20 @@ def test_prep_rejects_bad_arguments(cuda_ok):
     y = torch.zeros((1, 2, 128, 128), device=dev(), dtype=torch.bfloat16)[..., 1:]
     with pytest.raises(ValueError):
         K.pool_blocks(y, 2, 8, 8, (1, 8, 8))  # D=127 rows are not 16-byte vectors
+
+
+@pytest.mark.parametrize("dtype,D", [("bf16", 128), ("fp16", 64), ("fp32", 128)])
+def test_pool_blocks_normalized_equals_normalize_after_pool(cuda_ok, dtype, D):
+    """li_pool_blocks(normalized=1) == li_normalize_rows(li_pool_blocks(...)), bit for bit,
+    with a frame list and a block offset into an existing pool."""
+    B, H, T, LH, LW, tile = 1, 3, 8, 30, 52, (4, 4, 8)
+    x, tx = rand((B, H, 10 * LH * LW, D), 321, dtype)
+    ids = torch.tensor([9, 0, 3, 3, 7, 1, 2, 8], dtype=torch.int32, device=dev())
+    nblk = 2 * 8 * 7
+    raw = K.pool_blocks(tx, T, LH, LW, tile, frame_ids=ids)
+    want = K.normalize_rows(raw)
+    got = torch.full((B, H, nblk + 5, D), float("nan"), device=dev(), dtype=TORCH_DT[dtype])
+    K.pool_blocks(tx, T, LH, LW, tile, frame_ids=ids, normalized=True, out=got, block_offset=5)
+    torch.cuda.synchronize()
+    assert torch.equal(got[:, :, 5:], want)
+    assert torch.isnan(got[:, :, :5]).all()

@@ -61,6 +61,42 @@ def test_all_to_all_round_trip_two_ranks():
     assert res == [(0, True, True), (1, True, True)]
 
 
+def _qkv_worker(rank, world, port, result_q):
+    """The rank-major QKV projection lands in the layout seq_to_head produces
+    (integer-valued inputs, so every product and sum is exact in fp32)."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        from light_interaction_project_b200.ulysses import qkv_to_head, rank_major_qkv_weight, seq_to_head
+        S, hidden, H, D = 8, 12, 4, 16
+        g = torch.Generator().manual_seed(1)
+        x = torch.randint(-3, 4, (S, hidden), generator=g).float()
+        w = torch.randint(-3, 4, (hidden, 3 * H * D), generator=g).float()
+        s = S // world
+        mine = x[rank * s:(rank + 1) * s]
+        got = qkv_to_head(mine, rank_major_qkv_weight(w, world, H, D), world, H, D)
+        want = seq_to_head((mine @ w).view(1, s, 3, H, D).permute(2, 0, 1, 3, 4), world)
+        result_q.put((rank, tuple(got.shape) == tuple(want.shape) and torch.equal(got, want)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rank_major_qkv_projection_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_qkv_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    res = sorted(q.get(timeout=5) for _ in range(2))
+    assert all(p.exitcode == 0 for p in procs)
+    assert res == [(0, True), (1, True)]
+
+
 def _lonely(port, result_q):
     import datetime
     os.environ["MASTER_ADDR"] = "127.0.0.1"
