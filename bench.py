@@ -299,6 +299,10 @@ def run_gpu(args, cfg, rank, world, local_rank):
     ms_e2e = s2.elapsed_time(e2)
     K.raise_device_errors(dev)
 
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stack.close()
     # The host-side reference sample (rank 0, N=1 only, on every host core) runs
     # before the last collective, so every rank leaves the process group together.
     cpu = None

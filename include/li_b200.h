@@ -257,6 +257,45 @@ li_status li_sparse_attn_raster(const li_view4* q, li_grid3d grid_q,
                                 li_view4* o, float* lse, uint32_t* err_word,
                                 void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ---- (e) head-sharded stack: all-to-all over NVLink peer memory ----------
+ * No reference counterpart inside the sparse op; replaces the NCCL exchange of
+ * the upstream Ulysses re-layout (all_to_all_4D, hy patch:646-654,744-745)
+ * around it. Buffers are plain CUDA IPC allocations (no multicast object). */
+#define LI_A2A_MAX_RANKS    8
+#define LI_IPC_HANDLE_BYTES 64
+
+/* Setup-time only (not per call): a zeroed device allocation of `bytes` and
+ * its IPC handle (LI_IPC_HANDLE_BYTES bytes written to handle_out). */
+li_status li_ipc_alloc(int64_t bytes, void** ptr, void* handle_out);
+/* Maps a peer process's allocation from its IPC handle (peer access enabled). */
+li_status li_ipc_open(const void* handle, void** ptr);
+li_status li_ipc_close(void* ptr);
+li_status li_ipc_free(void* ptr);
+
+typedef struct li_a2a_desc {
+  const void* src;                      /* local send buffer                          */
+  int64_t src_chunk_stride;             /* bytes between the chunks for rank p        */
+  int64_t src_row_stride;               /* bytes between rows of a chunk              */
+  int64_t rows, row_bytes;              /* rows per chunk, bytes per row (x16)        */
+  void* dst[LI_A2A_MAX_RANKS];          /* receive buffer of every rank (IPC-mapped)  */
+  int64_t dst_bytes;                    /* size of each receive buffer                */
+  int64_t dst_offset;                   /* where this rank's chunk lands, bytes       */
+  int64_t dst_row_stride;               /* bytes between its rows there               */
+  uint32_t* flags[LI_A2A_MAX_RANKS];    /* flag array of every rank (world u32 each)  */
+  uint32_t* my_flags;                   /* this rank's flag array (= flags[rank])     */
+  uint32_t* counter;                    /* this rank's zeroed u32 ticket counter      */
+  uint32_t* err_word;                   /* optional device error word                 */
+  uint32_t epoch;                       /* 1, 2, ... per call, the same on all ranks  */
+  int32_t world, rank;
+} li_a2a_desc;
+
+/* Chunk p of `src` (rows x row_bytes) -> rank p's receive buffer at dst_offset,
+ * rows dst_row_stride apart, with 16-byte peer stores; returns (on the stream)
+ * once every rank's chunk for this rank has landed. Every rank must make the
+ * same sequence of calls; one descriptor's counter serves one stream. A peer
+ * that does not join within 2 s sets LI_DEVERR_TIMEOUT and the kernel returns. */
+li_status li_a2a_push(const li_a2a_desc* desc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,18 @@ class Grid3d(Structure):
     _fields_ = [("T", c_int32), ("LH", c_int32), ("LW", c_int32), ("tt", c_int32), ("th", c_int32), ("tw", c_int32)]
 
 
+A2A_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class A2ADesc(Structure):
+    _fields_ = [("src", c_void_p), ("src_chunk_stride", c_int64), ("src_row_stride", c_int64),
+                ("rows", c_int64), ("row_bytes", c_int64), ("dst", c_void_p * A2A_MAX_RANKS),
+                ("dst_bytes", c_int64), ("dst_offset", c_int64), ("dst_row_stride", c_int64),
+                ("flags", c_void_p * A2A_MAX_RANKS), ("my_flags", c_void_p), ("counter", c_void_p),
+                ("err_word", c_void_p), ("epoch", c_uint32), ("world", c_int32), ("rank", c_int32)]
+
+
 class SelectParams(Structure):
     _fields_ = [("mode", c_int32), ("metric", c_int32), ("tt", c_int32), ("th", c_int32), ("tw", c_int32),
                 ("grid_q", c_int32 * 3), ("grid_k", c_int32 * 3), ("text_len", c_int32),
@@ -84,6 +96,11 @@ SIGNATURES = {
                                  POINTER(IndexView), POINTER(View4), c_void_p], c_int32),
     "li_normalize_rows": ([POINTER(View4), POINTER(View4), c_void_p], c_int32),
     "li_rank_blocks": ([POINTER(View4), c_int32, c_int32, c_int32, c_int32, POINTER(IndexView), c_void_p], c_int32),
+    "li_ipc_alloc": ([c_int64, POINTER(c_void_p), c_void_p], c_int32),
+    "li_ipc_open": ([c_void_p, POINTER(c_void_p)], c_int32),
+    "li_ipc_close": ([c_void_p], c_int32),
+    "li_ipc_free": ([c_void_p], c_int32),
+    "li_a2a_push": ([POINTER(A2ADesc), c_void_p], c_int32),
     "li_sparse_attn_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, c_int32, POINTER(c_int64)], c_int32),
     "li_sparse_attn_tiled": ([POINTER(View4), POINTER(View4), POINTER(View4), POINTER(IndexView), c_int32, c_float,
                               POINTER(View4), c_void_p, c_void_p, c_void_p, c_int64, c_void_p], c_int32),

@@ -66,6 +66,100 @@ def qkv_to_head(x2d: torch.Tensor, w_rank_major: torch.Tensor, world: int, heads
     return recv.view(world * s, 3, 1, heads // world, head_dim)
 
 
+class _DeviceBuffer:
+    """A raw device allocation seen by torch through ``__cuda_array_interface__``."""
+
+    def __init__(self, ptr: int, nbytes: int, device_index: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes // 2,), "typestr": "<u2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self.device_index = device_index
+
+
+class PeerExchange:
+    """One all-to-all pattern over NVLink peer memory (``li_a2a_push``).
+
+    Each rank allocates two receive buffers (alternating by call parity) and a
+    flag array through CUDA IPC, exchanges the handles over the process group
+    once, and maps its peers' buffers. A call pushes chunk p of the send buffer
+    into rank p's receive buffer and returns, on the current stream, once this
+    rank's receive buffer is complete. Every rank must make the same calls in the
+    same order; one exchange serves one stream.
+    """
+
+    def __init__(self, recv_bytes: int, rank: int, world: int, device, group=None):
+        import ctypes
+        from . import _lib as L
+        if world > L.A2A_MAX_RANKS:
+            raise ValueError(f"peer exchange supports up to {L.A2A_MAX_RANKS} ranks")
+        self.L, self.lib = L, L.load()
+        self.rank, self.world, self.device, self.group = rank, world, torch.device(device), group
+        self.recv_bytes = (int(recv_bytes) + 255) // 256 * 256
+        self.own, self.mapped = [], []
+        handles = []
+        for nbytes in (self.recv_bytes, self.recv_bytes, 256):     # recv[0], recv[1], flags
+            ptr, h = ctypes.c_void_p(), (ctypes.c_char * L.IPC_HANDLE_BYTES)()
+            L.check(self.lib.li_ipc_alloc(nbytes, ctypes.byref(ptr), h), "li_ipc_alloc")
+            self.own.append(ptr.value)
+            handles.append(bytes(h))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, handles, group=group)
+        self.peers = []                                               # [rank][recv0, recv1, flags]
+        for p in range(world):
+            if p == rank:
+                self.peers.append(list(self.own))
+                continue
+            ptrs = []
+            for hb in gathered[p]:
+                ptr = ctypes.c_void_p()
+                L.check(self.lib.li_ipc_open(hb, ctypes.byref(ptr)), "li_ipc_open")
+                self.mapped.append(ptr.value)
+                ptrs.append(ptr.value)
+            self.peers.append(ptrs)
+        self.counter = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        self.views = [torch.as_tensor(_DeviceBuffer(self.own[i], self.recv_bytes, self.device.index),
+                                      device=self.device) for i in range(2)]
+        dist.barrier(group=group)
+
+    def recv_view(self, parity: int, dtype=torch.bfloat16) -> torch.Tensor:
+        return self.views[parity].view(dtype)
+
+    def push(self, src: torch.Tensor, rows: int, row_bytes: int, src_chunk_stride: int, src_row_stride: int,
+             dst_offset: int, dst_row_stride: int) -> torch.Tensor:
+        """Exchange; returns this rank's receive buffer (flat, dtype of ``src``)."""
+        L = self.L
+        if not src.is_cuda or src.device != self.device:
+            raise ValueError("send buffer must be on this rank's device")
+        span = (self.world - 1) * src_chunk_stride + (rows - 1) * src_row_stride + row_bytes
+        if not src.is_contiguous() or span > src.numel() * src.element_size():
+            raise ValueError("send buffer must be contiguous and cover the exchange pattern")
+        self.epoch += 1
+        parity = self.epoch & 1
+        d = L.A2ADesc()
+        d.src = src.data_ptr()
+        d.src_chunk_stride, d.src_row_stride = src_chunk_stride, src_row_stride
+        d.rows, d.row_bytes = rows, row_bytes
+        for p in range(self.world):
+            d.dst[p] = self.peers[p][parity]
+            d.flags[p] = self.peers[p][2]
+        d.dst_bytes, d.dst_offset, d.dst_row_stride = self.recv_bytes, dst_offset, dst_row_stride
+        d.my_flags = self.own[2]
+        d.counter = self.counter.data_ptr()
+        d.err_word = K.error_word(self.device).data_ptr()
+        d.epoch, d.world, d.rank = self.epoch & 0xFFFFFFFF, self.world, self.rank
+        L.check(self.lib.li_a2a_push(L.ptr(d), L.stream_ptr(self.device)), "li_a2a_push")
+        return self.recv_view(parity, src.dtype)
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (call after the last use
+        has completed on every rank)."""
+        for p in self.mapped:
+            self.lib.li_ipc_close(p)
+        for p in self.own:
+            self.lib.li_ipc_free(p)
+        self.mapped, self.own = [], []
+
+
 def head_to_seq(o: torch.Tensor, world: int, group=None) -> torch.Tensor:
     """``[B, H/P, S, D]`` (this rank's heads, all tokens) -> ``[B, S/P, H, D]``."""
     B, hl, S, D = o.shape
@@ -91,6 +185,7 @@ class StackConfig:
     keep_ratio: float = 0.25
     metric: str = "cosine"
     batch: int = 1
+    exchange: str = "peer"     # N > 1: "peer" (li_a2a_push over NVLink) or "nccl"
 
     @property
     def frame_tokens(self):
@@ -148,6 +243,14 @@ class HeadShardedStack:
         # N > 1, batch 1: the QKV projection writes the all-to-all send buffer directly.
         self.w_qkv_rank = ([rank_major_qkv_weight(w, world, cfg.heads, cfg.head_dim) for w in self.w_qkv]
                            if world > 1 and cfg.batch == 1 else None)
+        # N > 1, batch 1: both exchanges over NVLink peer memory; the output side lands
+        # directly in the [s, H, D] rows the O projection reads.
+        self.ex_qkv = self.ex_out = None
+        if world > 1 and cfg.batch == 1 and cfg.exchange == "peer":
+            s = cfg.q_tokens // world
+            es = 2
+            self.ex_qkv = PeerExchange(world * s * 3 * self.hl * cfg.head_dim * es, rank, world, self.device, group)
+            self.ex_out = PeerExchange(s * cfg.heads * cfg.head_dim * es, rank, world, self.device, group)
         kv_tokens = cfg.kv_frames * cfg.frame_tokens
         self.k_buf: List[torch.Tensor] = []
         self.v_buf: List[torch.Tensor] = []
@@ -178,7 +281,13 @@ class HeadShardedStack:
     def layer(self, i: int, x: torch.Tensor, attn_events=None) -> torch.Tensor:
         cfg = self.cfg
         B, s, _ = x.shape
-        if self.w_qkv_rank is not None:
+        if self.ex_qkv is not None:
+            send = torch.matmul(x.reshape(B * s, cfg.hidden), self.w_qkv_rank[i])   # [P, s, 3*hl*D]
+            row = 3 * self.hl * cfg.head_dim * send.element_size()
+            recv = self.ex_qkv.push(send, s, row, s * row, row, self.rank * s * row, row)
+            full = recv[: self.world * s * 3 * self.hl * cfg.head_dim].view(self.world * s, 3, 1, self.hl,
+                                                                                cfg.head_dim)
+        elif self.w_qkv_rank is not None:
             full = qkv_to_head(x.reshape(B * s, cfg.hidden), self.w_qkv_rank[i], self.world, cfg.heads,
                                cfg.head_dim, self.group)                         # [S, 3, B, hl, D]
         else:
@@ -200,9 +309,21 @@ class HeadShardedStack:
                                     q_block_offset=self.q_block_offset, out=o_tok.permute(0, 2, 1, 3), k_pool=kp)
         if attn_events is not None:
             attn_events[1].record()
-        back = head_to_seq(o, self.world, self.group)                           # [B, s, H, D]
+        if self.ex_out is not None:
+            row = self.hl * cfg.head_dim * o_tok.element_size()
+            recv = self.ex_out.push(o_tok, s, row, s * row, row, self.rank * row, cfg.heads * row // self.hl)
+            back = recv[: s * cfg.heads * cfg.head_dim].view(B, s, cfg.heads, cfg.head_dim)
+        else:
+            back = head_to_seq(o, self.world, self.group)                       # [B, s, H, D]
         out = back.reshape(B * s, cfg.heads * cfg.head_dim) @ self.w_o[i]
         return x + out.view(B, s, cfg.hidden)
+
+    def close(self):
+        """Releases the peer-exchange buffers (after the last step has completed on every rank)."""
+        for ex in (self.ex_qkv, self.ex_out):
+            if ex is not None:
+                ex.close()
+        self.ex_qkv = self.ex_out = None
 
     def step(self, x: torch.Tensor, attn_events=None) -> torch.Tensor:
         for i in range(self.cfg.layers):
