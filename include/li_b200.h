@@ -5,8 +5,9 @@
  * Every entry point takes plain device pointers, element strides, sizes and a
  * CUDA stream (passed as `void*`, i.e. a cudaStream_t / CUstream; NULL is the
  * legacy default stream). Calls are asynchronous on that stream, allocate no
- * memory, and never synchronise the host. Each returns an li_status; on a
- * non-zero status nothing was launched and li_last_error() describes why.
+ * memory (except the setup-time li_ipc_alloc), and never synchronise the host.
+ * Each returns an li_status; on a non-zero status nothing was launched and
+ * li_last_error() describes why.
  *
  * Tensor views (li_view4 / li_view5) describe strided tensors. Strides are in
  * elements. The innermost dimension (head dim D) must be contiguous.
