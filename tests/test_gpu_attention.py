@@ -355,3 +355,30 @@ def test_key_pool_cache_matches_full_pooling(cuda_ok):
         torch.cuda.synchronize()
         assert torch.equal(cache.selection_pool("cosine"), full), f"step {step}"
         assert torch.equal(got, want), f"step {step}"
+
+
+def test_many_tiles_random_lists(cuda_ok):
+    """320 query tiles (2 waves + tail on 148 SMs) with random per-tile lists (short,
+    empty, identical neighbours), checked against the oracle: whole tiles plus
+    tail pieces merged by the combine kernel."""
+    B, H, D, bs, nq, nkb, S = 1, 16, 128, 128, 20, 40, 24
+    q, tq = rand((B, H, nq * bs, D), 961, "bf16")
+    k, tk = rand((B, H, nkb * bs, D), 962, "bf16")
+    v, tv = rand((B, H, nkb * bs, D), 963, "bf16")
+    idx, cnt = _random_lists(np.random.default_rng(11), B, H, nq, nkb, S)
+    cnt[0, 0, 0] = 0          # an empty list paired with a full one
+    cnt[0, 1, 1] = 0          # and the other way round
+    cnt[0, 2, 2:4] = 0        # a pair of empty lists
+    idx[0, 3, 5] = idx[0, 3, 4]   # identical lists in one pair: every block shared
+    cnt[0, 3, 5] = cnt[0, 3, 4]
+    out, lse = K.sparse_attn_tiled(tq, tk, tv, torch.from_numpy(idx).to(dev()), torch.from_numpy(cnt).to(dev()),
+                                   bs, return_lse=True)
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    ref, ref_lse = O.sparse_attention_tiled(q.reshape(B, H, nq, bs, D), k.reshape(B, H, nkb, bs, D),
+                                            v.reshape(B, H, nkb, bs, D), idx, cnt, p_dtype="bf16")
+    assert_close_bf16(to_np(out), ref.reshape(B, H, nq * bs, D))
+    got_lse = to_np(lse)
+    fin = np.isfinite(ref_lse.reshape(B, H, -1))
+    np.testing.assert_allclose(got_lse[fin], ref_lse.reshape(B, H, -1)[fin], atol=2e-3, rtol=1e-4)
+    assert np.isneginf(got_lse[~fin]).all()
