@@ -423,13 +423,96 @@ def run_gpu_layer(args, rank, world, local_rank):
               flush=True)
 
 
+def run_configs(args):
+    """``--workload configs``: BASELINE configs 1-4 through the public operators on
+    one GPU (ms/call, executed TFLOP/s) beside the oracle's CPU path on a one-head
+    sample scaled to all heads. One JSON line per case. Synthetic seeded inputs
+    (no RoPE; the timing does not depend on the values)."""
+    from oracle import li_oracle as O
+    from light_interaction_project_b200 import ar_sparse_operation as ar
+    from light_interaction_project_b200 import bi_sparse_operation as mg
+    from light_interaction_project_b200 import kernels as K
+    from light_interaction_project_b200.pipeline import sparse_forward
+    from light_interaction_project_b200 import _lib as L
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L.load()
+    burst, _, kind = _peaks()
+    torch.set_num_threads(os.cpu_count() or 1)
+    hy = lambda tile, ratio, rp: dict(tile_size=tile, topk_ratio=ratio, recent_protect=rp,  # noqa: E731
+                                      sim_metric="scaled_dot_product")
+    cases = [("config1_toy", "hy", torch.float32, 4, 64, 8, 8, 2, 6, hy((2, 4, 8), 0.5, 2), False),
+             ("config2_hy", "hy", torch.bfloat16, 16, 128, 30, 52, 4, 16, hy((1, 8, 16), 0.25, 4), False),
+             ("config3_mg", "mg", torch.bfloat16, 24, 128, 30, 52, 4, 20,
+              dict(tile_size=(4, 4, 8), topk_ratio=0.30, sim_metric="cosine"), False)]
+    for mem in (8, 16, 32, 64):
+        for keep in (0.10, 0.25, 0.50, 1.00):
+            cases.append((f"config4_mem{mem}_keep{int(keep * 100)}", "hy", torch.bfloat16, 16, 128, 30, 52, 4, mem,
+                          hy((1, 8, 16), keep, 4), True))
+    for name, mode, dt, H, D, LH, LW, Fq, Fk, params, bias in cases:
+        HW = LH * LW
+        g = torch.Generator(device=dev).manual_seed(5)
+        q = torch.randn(1, H, Fq * HW, D, generator=g, device=dev).to(dt)
+        k = torch.randn(1, H, Fk * HW, D, generator=g, device=dev).to(dt)
+        v = torch.randn(1, H, Fk * HW, D, generator=g, device=dev).to(dt)
+        tile = params["tile_size"]
+        gq, gk = K.grid_blocks(Fq, LH, LW, tile), K.grid_blocks(Fk, LH, LW, tile)
+        nq, nk = int(np.prod(gq)), int(np.prod(gk))
+        bs = tile[0] * tile[1] * tile[2]
+        empty = q[:, :, :0]
+        sb = None
+        if bias:
+            rng = np.random.default_rng(7 + Fk)
+            sb = torch.from_numpy((0.01 * rng.lognormal(0.0, 1.0, size=(1, 1, 1, nk))).astype(np.float32)).to(dev)
+        smode = L.SELECT_BIDIR if mode == "mg" else L.SELECT_DECODE
+        sp = K.select_params(smode, params["sim_metric"], tile, gk if mode == "mg" else gq, gk, 0,
+                             params.get("recent_protect", 0), params["topk_ratio"], 7, nk - nq if mode == "mg" else 0)
+        sel = K.select_budget(sp, nq, nk)[1]          # the library's own budget rule
+        if mode == "mg":
+            call = lambda: mg.run_sparse_attention(q, k, v, 0, 0, (LH, LW), params, q_block_offset=nk - nq)  # noqa
+        elif bias:
+            call = lambda: sparse_forward(q, empty, empty, k, v, (LH, LW), params, L.SELECT_DECODE, tile,  # noqa
+                                          score_bias=sb)
+        else:
+            call = lambda: ar.run_sparse_attention(q, empty, empty, k, v, 0, (LH, LW), params)  # noqa
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            call()
+        b.record()
+        torch.cuda.synchronize()
+        K.raise_device_errors(dev)
+        ms = a.elapsed_time(b) / 10
+        fl = 4.0 * H * nq * bs * sel * bs * D
+        # CPU: the oracle's path (selection + dense masked SDPA) on head 0, scaled to H heads.
+        qn, kn, vn = (x[:, :1].float().cpu().numpy() for x in (q, k, v))
+        odt = "fp32" if dt == torch.float32 else "bf16"
+        t0 = time.perf_counter()
+        if mode == "mg":
+            O.run_sparse_attention_mg(qn, kn, vn, 0, (LH, LW), params, odt, q_offset=nk - nq)
+        else:
+            z = qn[:, :, :0]
+            O.run_sparse_attention_hy(qn, z, z, kn, vn, (LH, LW), params, odt)
+        cpu_ms = (time.perf_counter() - t0) * 1e3 * H
+        print(json.dumps({"workload": "configs", "case": name, "gpu_ms_per_call": round(ms, 4),
+                          "executed_tflop": fl / 1e12, "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+                          "frac_of_burst": round(fl / (ms * 1e-3) / 1e12 / burst, 3), "peak_kind": kind,
+                          "selected_per_q_block": sel, "q_blocks": nq, "k_blocks": nk, "heads": H,
+                          "cpu_ms_per_call": round(cpu_ms, 1), "cpu_sample": "head 0, scaled to all heads",
+                          "cpu_threads": torch.get_num_threads(), "cpu_count": os.cpu_count(),
+                          "score_bias": "lognormal(0,1)*0.01 per key block" if bias else None}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack", "mg_layer"])
+    ap.add_argument("--workload", default="stack", choices=["stack", "mg_layer", "configs"])
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--warmup-ref", type=int, default=0)
     args = ap.parse_args()
@@ -443,6 +526,10 @@ def main():
         return
     if args.workload == "mg_layer":
         run_gpu_layer(args, rank, world, local_rank)
+        return
+    if args.workload == "configs":
+        if rank == 0:
+            run_configs(args)
         return
     if world > 1:
         import datetime
