@@ -427,7 +427,13 @@ def run_configs(args):
     """``--workload configs``: BASELINE configs 1-4 through the public operators on
     one GPU (ms/call, executed TFLOP/s) beside the oracle's CPU path on a one-head
     sample scaled to all heads. One JSON line per case. Synthetic seeded inputs
-    (no RoPE; the timing does not depend on the values)."""
+    (no RoPE; the timing does not depend on the values).
+
+    The last case is the HY prefill / KV-recompute call at full context: q, k
+    and v cover the same 16 frames, B = 2 (the plain and ProPE streams), 256 text
+    tokens, and q handed over as ``query.transpose(1, 2)`` of a [B, S, H, D]
+    tensor, as the patched HY attention does."""
+    from light_interaction_project_b200 import bi_sparse_operation_for_KV_cache as hyp
     from oracle import li_oracle as O
     from light_interaction_project_b200 import ar_sparse_operation as ar
     from light_interaction_project_b200 import bi_sparse_operation as mg
@@ -449,12 +455,22 @@ def run_configs(args):
         for keep in (0.10, 0.25, 0.50, 1.00):
             cases.append((f"config4_mem{mem}_keep{int(keep * 100)}", "hy", torch.bfloat16, 16, 128, 30, 52, 4, mem,
                           hy((1, 8, 16), keep, 4), True))
+    cases.append(("f2_hy_prefill_b2_full_context", "hy_prefill", torch.bfloat16, 16, 128, 30, 52, 16, 16,
+                  dict(tile_size=(4, 8, 4), topk_ratio=0.3, sim_metric="scaled_dot_product"), False))
+    if args.cases:
+        cases = [c for c in cases if re.search(args.cases, c[0])]
     for name, mode, dt, H, D, LH, LW, Fq, Fk, params, bias in cases:
         HW = LH * LW
+        B, ntok_txt = (2, 256) if mode == "hy_prefill" else (1, 0)
         g = torch.Generator(device=dev).manual_seed(5)
-        q = torch.randn(1, H, Fq * HW, D, generator=g, device=dev).to(dt)
-        k = torch.randn(1, H, Fk * HW, D, generator=g, device=dev).to(dt)
-        v = torch.randn(1, H, Fk * HW, D, generator=g, device=dev).to(dt)
+        if mode == "hy_prefill":
+            q = torch.randn(B, Fq * HW, H, D, generator=g, device=dev).to(dt).transpose(1, 2)
+        else:
+            q = torch.randn(B, H, Fq * HW, D, generator=g, device=dev).to(dt)
+        k = torch.randn(B, H, Fk * HW, D, generator=g, device=dev).to(dt)
+        v = torch.randn(B, H, Fk * HW, D, generator=g, device=dev).to(dt)
+        kt = torch.randn(B, H, ntok_txt, D, generator=g, device=dev).to(dt)
+        vt = torch.randn(B, H, ntok_txt, D, generator=g, device=dev).to(dt)
         tile = params["tile_size"]
         gq, gk = K.grid_blocks(Fq, LH, LW, tile), K.grid_blocks(Fk, LH, LW, tile)
         nq, nk = int(np.prod(gq)), int(np.prod(gk))
@@ -464,11 +480,16 @@ def run_configs(args):
         if bias:
             rng = np.random.default_rng(7 + Fk)
             sb = torch.from_numpy((0.01 * rng.lognormal(0.0, 1.0, size=(1, 1, 1, nk))).astype(np.float32)).to(dev)
-        smode = L.SELECT_BIDIR if mode == "mg" else L.SELECT_DECODE
-        sp = K.select_params(smode, params["sim_metric"], tile, gk if mode == "mg" else gq, gk, 0,
+        smode = L.SELECT_DECODE if mode == "hy" else L.SELECT_BIDIR
+        sp = K.select_params(smode, params["sim_metric"], tile, gq if mode == "hy" else gk, gk, ntok_txt,
                              params.get("recent_protect", 0), params["topk_ratio"], 7, nk - nq if mode == "mg" else 0)
-        sel = K.select_budget(sp, nq, nk)[1]          # the library's own budget rule
-        if mode == "mg":
+        ntxt_blk, sel = K.select_budget(sp, nq, nk)   # the library's own budget rule
+        sel += ntxt_blk
+        if mode == "hy_prefill":
+            def call():
+                hyp.get_infer_state().current_chunk_index = 3
+                return hyp.run_sparse_prefill_attention(q, kt, vt, k, v, 0, (LH, LW), params)
+        elif mode == "mg":
             call = lambda: mg.run_sparse_attention(q, k, v, 0, 0, (LH, LW), params, q_block_offset=nk - nq)  # noqa
         elif bias:
             call = lambda: sparse_forward(q, empty, empty, k, v, (LH, LW), params, L.SELECT_DECODE, tile,  # noqa
@@ -486,22 +507,25 @@ def run_configs(args):
         torch.cuda.synchronize()
         K.raise_device_errors(dev)
         ms = a.elapsed_time(b) / 10
-        fl = 4.0 * H * nq * bs * sel * bs * D
-        # CPU: the oracle's path (selection + dense masked SDPA) on head 0, scaled to H heads.
-        qn, kn, vn = (x[:, :1].float().cpu().numpy() for x in (q, k, v))
+        fl = 4.0 * B * H * nq * bs * sel * bs * D
+        # CPU: the oracle's path (selection + dense masked SDPA) on batch 0, head 0,
+        # scaled to B * H heads.
+        qn, kn, vn, ktn, vtn = (x[:1, :1].float().cpu().numpy() for x in (q, k, v, kt, vt))
         odt = "fp32" if dt == torch.float32 else "bf16"
         t0 = time.perf_counter()
         if mode == "mg":
             O.run_sparse_attention_mg(qn, kn, vn, 0, (LH, LW), params, odt, q_offset=nk - nq)
+        elif mode == "hy_prefill":
+            O.run_sparse_prefill_attention_hy(qn, ktn, vtn, kn, vn, (LH, LW), params, odt)
         else:
-            z = qn[:, :, :0]
-            O.run_sparse_attention_hy(qn, z, z, kn, vn, (LH, LW), params, odt)
-        cpu_ms = (time.perf_counter() - t0) * 1e3 * H
+            O.run_sparse_attention_hy(qn, ktn, vtn, kn, vn, (LH, LW), params, odt)
+        cpu_ms = (time.perf_counter() - t0) * 1e3 * B * H
         print(json.dumps({"workload": "configs", "case": name, "gpu_ms_per_call": round(ms, 4),
                           "executed_tflop": fl / 1e12, "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
                           "frac_of_burst": round(fl / (ms * 1e-3) / 1e12 / burst, 3), "peak_kind": kind,
-                          "selected_per_q_block": sel, "q_blocks": nq, "k_blocks": nk, "heads": H,
-                          "cpu_ms_per_call": round(cpu_ms, 1), "cpu_sample": "head 0, scaled to all heads",
+                          "selected_per_q_block": sel, "q_blocks": nq, "k_blocks": nk, "heads": H, "batch": B,
+                          "text_tokens": ntok_txt,
+                          "cpu_ms_per_call": round(cpu_ms, 1), "cpu_sample": "batch 0 head 0, scaled to B*H",
                           "cpu_threads": torch.get_num_threads(), "cpu_count": os.cpu_count(),
                           "score_bias": "lognormal(0,1)*0.01 per key block" if bias else None}), flush=True)
 
@@ -515,6 +539,7 @@ def main():
     ap.add_argument("--workload", default="stack", choices=["stack", "mg_layer", "configs"])
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--warmup-ref", type=int, default=0)
+    ap.add_argument("--cases", default="", help="--workload configs: regex selecting case names")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

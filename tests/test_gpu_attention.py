@@ -168,6 +168,29 @@ def test_hy_transposed_views_and_batch2(cuda_ok):
     assert_close_bf16(to_np(out), ref)
 
 
+def test_hy_prefill_full_context_batch2(cuda_ok):
+    """The HY KV-recompute call: q, k and v cover the same frames, B = 2 (plain +
+    ProPE), text tokens in front, q a ``transpose(1, 2)`` view of [B, S, H, D]
+    (``hy patch:638-640, 705-727``)."""
+    B, H, D, LH, LW, F, T = 2, 2, 128, 12, 20, 8, 37
+    S = F * LH * LW
+    qb, tqb = rand((B, S, H, D), 811, "bf16")
+    kv, tkv = rand((B, H, S, D), 812, "bf16")
+    vv, tvv = rand((B, H, S, D), 813, "bf16")
+    kt, tkt = rand((B, H, T, D), 814, "bf16")
+    vt, tvt = rand((B, H, T, D), 815, "bf16")
+    params = dict(tile_size=(4, 8, 4), topk_ratio=0.3, sim_metric="scaled_dot_product")
+    hyp.get_infer_state().current_chunk_index = 5
+    try:
+        out = hyp.run_sparse_prefill_attention(tqb.transpose(1, 2), tkt, tvt, tkv, tvv, 2, (LH, LW), params)
+    finally:
+        hyp.get_infer_state().current_chunk_index = 0
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    ref, _ = O.run_sparse_prefill_attention_hy(qb.transpose(0, 2, 1, 3), kt, vt, kv, vv, (LH, LW), params, "bf16")
+    assert_close_bf16(to_np(out), ref, what="hy prefill B=2")
+
+
 @pytest.mark.parametrize("name", [c for c in list_cases() if not c.startswith("sel_")])
 def test_reference_fixtures_end_to_end(cuda_ok, name):
     """Reference inputs through the drop-in orchestrators vs the reference's
