@@ -225,7 +225,9 @@ def workload_config(cfg, args, world):
             "memory_frames": cfg.memory_frames, "tile": list(cfg.tile), "keep_ratio": cfg.keep_ratio,
             "sim_metric": cfg.metric, "q_blocks": nq, "k_blocks": nk, "selected_blocks": cfg.budget(),
             "attn_tflop_per_call": cfg.attention_flops() / 1e12,
-            "parallelism": f"ulysses_heads{world}", "l2": "inputs larger than L2 (resident K/V >> 126 MB)"}
+            "parallelism": f"ulysses_heads{world}", "l2": "inputs larger than L2 (resident K/V >> 126 MB)",
+            "exchange": cfg.exchange if world > 1 else None,
+            "cuda_graph": bool(getattr(args, "graph", False)) and args.workload == "stack"}
 
 
 # ---------------------------------------------------------------------------
@@ -268,21 +270,40 @@ def run_gpu(args, cfg, rank, world, local_rank):
         stack.step(x0)
     barrier()
     K.raise_device_errors(dev)
+    # With --graph (the default) the whole 30-layer step is one CUDA graph: x0 is
+    # its static input, refilled in place for the end-to-end leg. Every kernel and
+    # exchange of every layer still runs on each replay.
+    if args.graph:
+        stack.capture(x0)
+        per_step_launches = stack.graph_launches
+        barrier()
+        run_step = lambda: stack.replay()  # noqa: E731
+    else:
+        run_step = lambda: stack.step(x0)  # noqa: E731
+    run_step()
+    barrier()
 
-    # Device-resident timing, with the attention kernel's events on the last step.
+    # Device-resident timing.
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     launches0 = L.kernel_launches()
     with ClockSampler(local_rank) as clk:
         start.record()
         for s in range(args.steps):
-            attn_timing["on"] = s == args.steps - 1
-            stack.step(x0)
+            attn_timing["on"] = not args.graph and s == args.steps - 1
+            run_step()
         end.record()
         barrier()
     attn_timing["on"] = False
-    n_launch = L.kernel_launches() - launches0
+    n_launch = per_step_launches * args.steps if args.graph else L.kernel_launches() - launches0
     ms = start.elapsed_time(end)
+    if args.graph:
+        # The attention kernel's events come from one eager step (same kernels,
+        # same inputs) after the timed region.
+        attn_timing["on"] = True
+        stack.step(x0)
+        attn_timing["on"] = False
+        barrier()
     attn_ms = [a.elapsed_time(b) for a, b in attn_timing["events"]]
     # End-to-end: host input -> device, step, device output -> host.
     x_host = x0.cpu().pin_memory()
@@ -291,8 +312,12 @@ def run_gpu(args, cfg, rank, world, local_rank):
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record()
     for _ in range(args.steps):
-        xd = x_host.to(dev, non_blocking=True)
-        y = stack.step(xd)
+        if args.graph:
+            x0.copy_(x_host, non_blocking=True)
+            y = stack.replay()
+        else:
+            xd = x_host.to(dev, non_blocking=True)
+            y = stack.step(xd)
         y_host.copy_(y, non_blocking=True)
     e2.record()
     barrier()
@@ -540,12 +565,16 @@ def main():
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--warmup-ref", type=int, default=0)
     ap.add_argument("--cases", default="", help="--workload configs: regex selecting case names")
+    ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
+                    help="stack: run each step as one captured CUDA graph (--no-graph: eager launches)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="stack, N > 1: all-to-all over NVLink peer memory (li_a2a_push) or NCCL")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     from light_interaction_project_b200.ulysses import StackConfig
-    cfg = StackConfig(layers=args.layers)
+    cfg = StackConfig(layers=args.layers, exchange=args.exchange)
     if args.impl == "reference":
         run_reference(args, cfg, rank, world)
         return

@@ -286,6 +286,7 @@ typedef struct li_a2a_desc {
   uint32_t* my_flags;                   /* this rank's flag array (= flags[rank])     */
   uint32_t* counter;                    /* this rank's zeroed u32 ticket counter      */
   uint32_t* err_word;                   /* optional device error word                 */
+  uint32_t* epoch_word;                 /* optional: the epoch kept on the device     */
   uint32_t epoch;                       /* 1, 2, ... per call, the same on all ranks  */
   int32_t world, rank;
 } li_a2a_desc;
@@ -294,7 +295,11 @@ typedef struct li_a2a_desc {
  * rows dst_row_stride apart, with 16-byte peer stores; returns (on the stream)
  * once every rank's chunk for this rank has landed. Every rank must make the
  * same sequence of calls; one descriptor's counter serves one stream. A peer
- * that does not join within 2 s sets LI_DEVERR_TIMEOUT and the kernel returns. */
+ * that does not join within 2 s sets LI_DEVERR_TIMEOUT and the kernel returns.
+ * With `epoch_word` set (a zeroed u32 on this rank's device) the call's epoch is
+ * *epoch_word + 1, read and stored back by the kernel, and `epoch` is ignored:
+ * the launch then carries no per-call value, so a captured CUDA graph can replay
+ * it. */
 li_status li_a2a_push(const li_a2a_desc* desc, void* stream);
 
 #ifdef __cplusplus

@@ -38,6 +38,7 @@ struct A2AArgs {
   uint32_t* my_flags;
   uint32_t* counter;
   uint32_t* err;
+  uint32_t* epoch_word;  // optional: epoch = *epoch_word + 1, stored back at the end
   uint32_t epoch;
   int32_t world, rank;
 };
@@ -59,13 +60,21 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __global__ void __launch_bounds__(kA2AThreads) a2a_push_kernel(const A2AArgs a) {
   const int64_t v_per_row = a.row_bytes / 16;
   const int64_t v_per_chunk = a.rows * v_per_row;
-  const int64_t total = (int64_t)a.world * v_per_chunk;
-  for (int64_t i = (int64_t)blockIdx.x * kA2AThreads + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * kA2AThreads) {
-    const int p = (int)(i / v_per_chunk);
-    const int64_t r = (i % v_per_chunk) / v_per_row, c = i % v_per_row;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.src + p * a.src_chunk_stride + r * a.src_row_stride) + c);
-    *(reinterpret_cast<uint4*>(a.dst[p] + a.dst_offset + r * a.dst_row_stride) + c) = v;
+  // CTAs are dealt round-robin over the destinations, starting with the rank
+  // after this one: every rank writes to all of its peers at once and every rank
+  // receives from all of them at once. (Walking the chunks in order would send
+  // every rank's traffic to the same destination at the same time.)
+  const int W = a.world;
+  const int slot = (int)(blockIdx.x % W);
+  const int p = (a.rank + 1 + slot) % W;
+  const int64_t n_cta = (gridDim.x - slot + W - 1) / W;  // CTAs serving this destination
+  const uint8_t* src = a.src + p * a.src_chunk_stride;
+  uint8_t* dst = a.dst[p] + a.dst_offset;
+  for (int64_t i = (int64_t)(blockIdx.x / W) * kA2AThreads + threadIdx.x; i < v_per_chunk;
+       i += n_cta * kA2AThreads) {
+    const int64_t r = i / v_per_row, c = i % v_per_row;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + r * a.src_row_stride) + c);
+    *(reinterpret_cast<uint4*>(dst + r * a.dst_row_stride) + c) = v;
   }
   __threadfence_system();
   __syncthreads();
@@ -73,21 +82,27 @@ __global__ void __launch_bounds__(kA2AThreads) a2a_push_kernel(const A2AArgs a) 
   const uint32_t ticket = atomicAdd(a.counter, 1u);
   if (ticket != gridDim.x - 1) return;
   // Last CTA: every CTA's stores are fenced. Publish, then wait for the peers.
+  // Only this CTA uses the epoch, so a device-held epoch is read here (the
+  // previous call on this stream stored it before this launch began).
+  const uint32_t epoch = a.epoch_word ? *(volatile uint32_t*)a.epoch_word + 1u : a.epoch;
   __threadfence_system();
-  for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + a.rank, a.epoch);
+  for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + a.rank, epoch);
   const uint64_t t0 = a2a_timer();
-  for (int p = 0; p < a.world; ++p) {
+  bool timed_out = false;
+  for (int p = 0; p < a.world && !timed_out; ++p) {
     uint32_t it = 0;
     // A peer that already finished this call may have raised the next epoch:
     // accept any flag at or past this one (wrap-around compare).
-    while ((int32_t)(ld_acquire_sys(a.my_flags + p) - a.epoch) < 0) {
+    while ((int32_t)(ld_acquire_sys(a.my_flags + p) - epoch) < 0) {
       if ((++it & 63u) == 0 && a2a_timer() - t0 > kA2ATimeoutNs) {
         if (a.err) atomicOr(a.err, (unsigned)LI_DEVERR_TIMEOUT);
-        *a.counter = 0u;
-        return;
+        timed_out = true;
+        break;
       }
     }
   }
+  // The epoch advances on timeout too, so later calls stay numbered like the peers'.
+  if (a.epoch_word) *a.epoch_word = epoch;
   *a.counter = 0u;  // ready for the next call on this stream
 }
 
@@ -155,13 +170,15 @@ extern "C" li_status li_a2a_push(const li_a2a_desc* d, void* stream) {
   }
   a.dst_offset = d->dst_offset; a.dst_row_stride = d->dst_row_stride;
   a.rows = d->rows; a.row_bytes = d->row_bytes;
-  a.my_flags = d->my_flags; a.counter = d->counter; a.err = d->err_word;
+  a.my_flags = d->my_flags; a.counter = d->counter; a.err = d->err_word; a.epoch_word = d->epoch_word;
   a.epoch = d->epoch; a.world = d->world; a.rank = d->rank;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // A multiple of world CTAs, at least one per destination, about four vectors
+  // per thread, at most four CTAs per SM.
   const int64_t vecs = (int64_t)d->world * d->rows * (d->row_bytes / 16);
-  const int64_t want = ceil_div(vecs, (int64_t)kA2AThreads * 4);
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 4));
+  const int64_t want = std::min<int64_t>(ceil_div(vecs, (int64_t)kA2AThreads * 4), (int64_t)sms * 4);
+  const unsigned grid = (unsigned)(std::max<int64_t>(1, want / d->world) * d->world);
   a2a_push_kernel<<<grid, kA2AThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launched("a2a_push_kernel launch");
 }

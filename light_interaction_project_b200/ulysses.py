@@ -26,6 +26,7 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import bi_sparse_operation as mg
 from . import kernels as K
 from .memory import KeyPoolCache
@@ -146,6 +147,9 @@ class PeerExchange:
         d.my_flags = self.own[2]
         d.counter = self.counter.data_ptr()
         d.err_word = K.error_word(self.device).data_ptr()
+        # The epoch lives on the device (counter[1]); the host count only picks the
+        # receive buffer, so a captured graph replays with fresh epochs.
+        d.epoch_word = self.counter.data_ptr() + 4
         d.epoch, d.world, d.rank = self.epoch & 0xFFFFFFFF, self.world, self.rank
         L.check(self.lib.li_a2a_push(L.ptr(d), L.stream_ptr(self.device)), "li_a2a_push")
         return self.recv_view(parity, src.dtype)
@@ -254,13 +258,16 @@ class HeadShardedStack:
             self.ex_qkv = PeerExchange(world * s * 3 * self.hl * cfg.head_dim * es, rank, world, self.device, group)
             self.ex_out = PeerExchange(s * cfg.heads * cfg.head_dim * es, rank, world, self.device, group)
         kv_tokens = cfg.kv_frames * cfg.frame_tokens
+        # K and V of a layer share one allocation [B, 2, H/P, L, D], so the current
+        # chunk's K and V are written by one gather launch (heads of K, then of V).
+        self.kv_buf: List[torch.Tensor] = []
         self.k_buf: List[torch.Tensor] = []
         self.v_buf: List[torch.Tensor] = []
         for _ in range(cfg.layers):
-            self.k_buf.append(torch.randn(cfg.batch, self.hl, kv_tokens, cfg.head_dim, generator=g,
-                                          device=self.device).to(dt))
-            self.v_buf.append(torch.randn(cfg.batch, self.hl, kv_tokens, cfg.head_dim, generator=g,
-                                          device=self.device).to(dt))
+            kv = torch.randn(cfg.batch, 2, self.hl, kv_tokens, cfg.head_dim, generator=g, device=self.device).to(dt)
+            self.kv_buf.append(kv)
+            self.k_buf.append(kv[:, 0])
+            self.v_buf.append(kv[:, 1])
         nq, nk = cfg.blocks()
         self.q_block_offset = nk - nq
         # Identity frame list: the current chunk's K/V go into the buffer tail
@@ -270,6 +277,8 @@ class HeadShardedStack:
         # re-pools only the current chunk's block rows.
         self.key_pools = [KeyPoolCache(cfg.latent_hw, cfg.tile, cfg.metric) for _ in range(cfg.layers)]
         self.params = {"tile_size": tuple(cfg.tile), "topk_ratio": cfg.keep_ratio, "sim_metric": cfg.metric}
+        self._graph = None
+        self.graph_launches = 0
 
     def local_tokens(self):
         return self.cfg.q_tokens // self.world
@@ -299,8 +308,14 @@ class HeadShardedStack:
         q = full[:, 0].permute(1, 2, 0, 3)                                       # [B, hl, S, D] view
         tail = self.k_buf[i].shape[2] - S
         ft = cfg.frame_tokens
-        K.gather_frames(full[:, 1].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.k_buf[i][:, :, tail:])
-        K.gather_frames(full[:, 2].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.v_buf[i][:, :, tail:])
+        if B == 1:
+            # [S, 2, 1, hl, D] -> [1, 2*hl, S, D]: K heads then V heads, one launch.
+            src = full[:, 1:3].permute(2, 1, 3, 0, 4).view(1, 2 * self.hl, S, cfg.head_dim)
+            dst = self.kv_buf[i].view(1, 2 * self.hl, -1, cfg.head_dim)[:, :, tail:]
+            K.gather_frames(src, self.chunk_frames, ft, out=dst)
+        else:
+            K.gather_frames(full[:, 1].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.k_buf[i][:, :, tail:])
+            K.gather_frames(full[:, 2].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.v_buf[i][:, :, tail:])
         # The attention writes its output token-major ([B, S, H/P, D]), the order the
         # return all-to-all / O projection reads, so no re-layout copy follows.
         o_tok = torch.empty(B, S, self.hl, cfg.head_dim, device=x.device, dtype=x.dtype)
@@ -317,11 +332,14 @@ class HeadShardedStack:
             back = recv[: s * cfg.heads * cfg.head_dim].view(B, s, cfg.heads, cfg.head_dim)
         else:
             back = head_to_seq(o, self.world, self.group)                       # [B, s, H, D]
-        out = back.reshape(B * s, cfg.heads * cfg.head_dim) @ self.w_o[i]
-        return x + out.view(B, s, cfg.hidden)
+        # O projection with the residual add in the GEMM epilogue.
+        return torch.addmm(x.reshape(B * s, cfg.hidden), back.reshape(B * s, cfg.heads * cfg.head_dim),
+                           self.w_o[i]).view(B, s, cfg.hidden)
 
     def close(self):
-        """Releases the peer-exchange buffers (after the last step has completed on every rank)."""
+        """Releases the captured graph and the peer-exchange buffers (after the last
+        step has completed on every rank)."""
+        self._graph = None
         for ex in (self.ex_qkv, self.ex_out):
             if ex is not None:
                 ex.close()
@@ -331,3 +349,45 @@ class HeadShardedStack:
         for i in range(self.cfg.layers):
             x = self.layer(i, x, attn_events[i] if attn_events is not None else None)
         return x
+
+    def capture(self, x: torch.Tensor, warmup: int = 2) -> torch.Tensor:
+        """Records one :meth:`step` on the static input ``x`` into a CUDA graph and
+        returns its static output; :meth:`replay` then runs the whole step (every
+        kernel and exchange of every layer) as one graph launch. Refill ``x`` in
+        place between replays. The warm-up steps run first on a side stream, so
+        the key pools, workspaces and communicators exist before capture.
+
+        Every rank captures the same steps. The peer exchanges keep their epoch on
+        the device, and each alternates its two receive buffers by call parity, so
+        a graph must contain an even number of calls per exchange (one per layer:
+        an even layer count)."""
+        dev = self.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(x)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        exchanges = [ex for ex in (self.ex_qkv, self.ex_out) if ex is not None]
+        before = [ex.epoch for ex in exchanges]
+        graph = torch.cuda.CUDAGraph()
+        n0 = L.kernel_launches()
+        with torch.cuda.graph(graph):
+            y = self.step(x)
+        # library kernels one replay launches
+        self.graph_launches = L.kernel_launches() - n0
+        if any((ex.epoch - e0) % 2 for ex, e0 in zip(exchanges, before)):
+            raise ValueError("a captured step must make an even number of calls per peer exchange")
+        self._graph = (graph, y)
+        return y
+
+    def replay(self) -> torch.Tensor:
+        """Runs the captured step on the current contents of its static input."""
+        if self._graph is None:
+            raise RuntimeError("HeadShardedStack.capture() has not been called")
+        self._graph[0].replay()
+        return self._graph[1]
+
+    def release_graph(self):
+        """Drops the captured graph (before the process group is destroyed)."""
+        self._graph = None

@@ -114,3 +114,52 @@ def test_tensor_wrappers_refuse_cpu_tensors():
     import torch
     with pytest.raises(ValueError, match="CUDA"):
         L.view4(torch.zeros(1, 1, 1, 8), "x")
+
+
+_STRUCTS = {"li_view4": L.View4, "li_view5": L.View5, "li_index_view": L.IndexView, "li_grid3d": L.Grid3d,
+            "li_select_params": L.SelectParams, "li_a2a_desc": L.A2ADesc}
+
+
+def test_ctypes_structs_match_header_layout(tmp_path):
+    """Field order, offsets and sizes of every C-ABI struct, as gcc lays them out
+    from the header, equal the ctypes mirrors."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
+    for cname, cls in _STRUCTS.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'printf("{cname} {fname} %zu %zu\\n", offsetof({cname}, {fname}), '
+                         f'sizeof((({cname}*)0)->{fname}));')
+    lines += ["return 0;", "}"]
+    src, exe = tmp_path / "layout.c", tmp_path / "layout"
+    src.write_text("\n".join(lines))
+    subprocess.run(["gcc", "-std=c11", "-o", str(exe), str(src)], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {}
+    for row in out:
+        parts = row.split()
+        if len(parts) == 3:
+            got[(parts[0], "__size__")] = int(parts[2])
+        elif len(parts) == 4:
+            got[(parts[0], parts[1])] = (int(parts[2]), int(parts[3]))
+    for cname, cls in _STRUCTS.items():
+        assert got[(cname, "__size__")] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            f = getattr(cls, fname)
+            assert got[(cname, fname)] == (f.offset, f.size), f"{cname}.{fname}"
+    # every header field is mirrored (no field missing from a ctypes struct)
+    text = open(HEADER).read()
+    for cname, cls in _STRUCTS.items():
+        body = re.search(r"typedef struct " + cname + r" \{(.*?)\} " + cname + ";", text, flags=re.S).group(1)
+        body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        names = []
+        for decl in body.split(";"):
+            decl = decl.strip()
+            if not decl:
+                continue
+            for part in decl.split(","):
+                names.append(re.sub(r"\[.*?\]", "", part).replace("*", " ").split()[-1])
+        assert names == [n for n, _ in cls._fields_], cname

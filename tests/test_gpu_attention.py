@@ -347,12 +347,40 @@ def test_stack_layer_matches_plain_restatement(cuda_ok):
         v_ref[i][:, :, tail:].copy_(qkv[:, :, 2].permute(0, 2, 1, 3))
         o = mg.run_sparse_attention(q, k_ref[i], v_ref[i], 0, i, cfg.latent_hw, stack.params,
                                     q_block_offset=nk - nq)
-        out = o.permute(0, 2, 1, 3).reshape(B * s, cfg.heads * cfg.head_dim) @ stack.w_o[i]
-        xr = xr + out.view(B, s, cfg.hidden)
+        xr = torch.addmm(xr.reshape(B * s, cfg.hidden), o.permute(0, 2, 1, 3).reshape(B * s, cfg.heads * cfg.head_dim),
+                         stack.w_o[i]).view(B, s, cfg.hidden)
     torch.cuda.synchronize()
     for i in range(cfg.layers):
         assert torch.equal(stack.k_buf[i], k_ref[i]) and torch.equal(stack.v_buf[i], v_ref[i])
     assert torch.equal(y, xr)
+
+
+def test_stack_graph_replay_matches_eager(cuda_ok):
+    """HeadShardedStack.capture/replay at N=1: the captured step equals eager steps
+    bit for bit, and a replay after refilling the static input computes on the
+    new input."""
+    from light_interaction_project_b200.ulysses import HeadShardedStack, StackConfig
+    cfg = StackConfig(layers=2, heads=4, hidden=512, memory_frames=4)
+    stack = HeadShardedStack(cfg, 0, 1, dev())
+    x = stack.make_input(seed=3)
+    x2 = stack.make_input(seed=4)
+    y1 = stack.step(x).clone()
+    y2 = stack.step(x2).clone()
+    xs = x.clone()
+    n0 = L.kernel_launches()
+    ys = stack.capture(xs)
+    assert 0 < stack.graph_launches < L.kernel_launches() - n0     # the warm-up steps are not counted
+    stack.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(ys, y1)
+    xs.copy_(x2)
+    stack.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(ys, y2)
+    assert K.device_errors() == 0
+    stack.close()
+    with pytest.raises(RuntimeError):
+        stack.replay()
 
 
 def test_key_pool_cache_matches_full_pooling(cuda_ok):

@@ -1,5 +1,6 @@
 """Peer exchange (li_a2a_push over NVLink) on two GPUs: a head-sharded stack
-step gives bit-identical outputs through the peer exchange and through NCCL.
+step gives bit-identical outputs through the peer exchange and through NCCL,
+eagerly and replayed from a captured CUDA graph.
 Needs two GPUs (skipped otherwise); each rank is its own process."""
 
 import os
@@ -34,16 +35,24 @@ def _rank(rank, world, port, q):
         from light_interaction_project_b200.ulysses import HeadShardedStack, StackConfig
         outs = {}
         for mode in ("peer", "nccl"):
-            cfg = StackConfig(layers=3, heads=4, hidden=512, memory_frames=4, exchange=mode)
+            cfg = StackConfig(layers=2, heads=4, hidden=512, memory_frames=4, exchange=mode)
             st = HeadShardedStack(cfg, rank, world, dev, group=dist.group.WORLD)
             x = st.make_input()
             ys = [st.step(x) for _ in range(2)]       # two steps: both buffer parities, rising epochs
+            # The same step as a captured CUDA graph (device-held epochs), replayed twice.
+            xs = x.clone()
+            yg = st.capture(xs)
+            for _ in range(2):
+                st.replay()
+                torch.cuda.synchronize()
+                ys.append(yg.clone())
             torch.cuda.synchronize()
             dist.barrier()
             st.close()
             outs[mode] = ys
         errs = K.device_errors(dev)
         same = all(torch.equal(a, b) for a, b in zip(outs["peer"], outs["nccl"]))
+        same = same and all(torch.equal(outs[m][0], y) for m in outs for y in outs[m][1:])
         q.put((rank, same, int(errs)))
     finally:
         dist.destroy_process_group()
