@@ -71,3 +71,75 @@ def test_peer_exchange_matches_nccl_two_gpus():
     assert all(p.exitcode == 0 for p in procs)
     res = sorted(q.get(timeout=5) for _ in range(2))
     assert res == [(0, True, 0), (1, True, 0)]
+
+
+def _desc(L, K, src, dsts, flags, counter, rows, row_bytes, world, rank, dev):
+    d = L.A2ADesc()
+    d.src = src.data_ptr()
+    d.src_chunk_stride, d.src_row_stride = rows * row_bytes, row_bytes
+    d.rows, d.row_bytes = rows, row_bytes
+    for p in range(world):
+        d.dst[p] = dsts[p].data_ptr()
+        d.flags[p] = flags[p].data_ptr()
+    d.dst_bytes = dsts[0].numel() * dsts[0].element_size()
+    d.dst_offset, d.dst_row_stride = 0, row_bytes
+    d.my_flags = flags[rank].data_ptr()
+    d.counter = counter.data_ptr()
+    d.err_word = K.error_word(dev).data_ptr()
+    d.epoch_word = counter.data_ptr() + 4
+    d.epoch, d.world, d.rank = 0, world, rank
+    return d
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_exchange_single_rank_completes():
+    """world = 1: the push copies the one chunk into this rank's buffer and its own
+    flag completes the barrier at once; the device epoch advances per call."""
+    from light_interaction_project_b200 import _lib as L
+    from light_interaction_project_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    K.device_errors(dev)
+    rows, row_bytes = 37, 96
+    src = torch.randint(0, 255, (rows * row_bytes,), dtype=torch.uint8, device=dev)
+    dst = torch.zeros_like(src)
+    flags = torch.zeros(4, dtype=torch.int32, device=dev)
+    counter = torch.zeros(4, dtype=torch.int32, device=dev)
+    lib = L.load()
+    for call in range(1, 4):
+        d = _desc(L, K, src, [dst], [flags], counter, rows, row_bytes, 1, 0, dev)
+        L.check(lib.li_a2a_push(L.ptr(d), L.stream_ptr(dev)), "li_a2a_push")
+        torch.cuda.synchronize()
+        assert counter[1].item() == call and flags[0].item() == call and counter[0].item() == 0
+    assert torch.equal(dst, src)
+    assert K.device_errors(dev) == 0
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_exchange_wait_runs_out_and_reports():
+    """A peer that never joins: rank 0 of a world of 2 on one GPU, with nothing
+    playing rank 1. The push still delivers both chunks (both buffers are local),
+    raises its flags, and its bounded wait for rank 1's flag gives up after 2 s:
+    LI_DEVERR_TIMEOUT in the error word, the epoch advanced, the context usable."""
+    import time
+    from light_interaction_project_b200 import _lib as L
+    from light_interaction_project_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    K.device_errors(dev)
+    rows, row_bytes = 64, 256
+    src = torch.randint(0, 255, (2 * rows * row_bytes,), dtype=torch.uint8, device=dev)
+    dsts = [torch.zeros(rows * row_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    flags = [torch.zeros(4, dtype=torch.int32, device=dev) for _ in range(2)]
+    counter = torch.zeros(4, dtype=torch.int32, device=dev)
+    d = _desc(L, K, src, dsts, flags, counter, rows, row_bytes, 2, 0, dev)
+    t0 = time.perf_counter()
+    L.check(L.load().li_a2a_push(L.ptr(d), L.stream_ptr(dev)), "li_a2a_push")
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert 1.5 < waited < 30.0
+    assert K.device_errors(dev) & L.LI_DEVERR_TIMEOUT
+    assert torch.equal(dsts[0], src[: rows * row_bytes]) and torch.equal(dsts[1], src[rows * row_bytes:])
+    assert flags[0][0].item() == 1 and flags[1][0].item() == 1 and flags[0][1].item() == 0
+    assert counter[1].item() == 1 and counter[0].item() == 0
+    # the context is still usable
+    x = torch.arange(1000, device=dev, dtype=torch.float32)
+    assert float((x * 2).sum().item()) == 999000.0
