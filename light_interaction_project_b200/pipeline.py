@@ -4,14 +4,18 @@ Reference stages (``ar_sparse_operation.py:289-362``): allocate tiled Q/K/V +
 pools, copy padded text K/V, tile+pool Q and K/V (Triton), select blocks
 (torch), block-sparse attention on the tiled tensors (Triton), untile. Here:
 
-1. ``li_tile_pool`` (pool only) writes the q and k block means — the tiled
-   copies are never materialised;
-2. ``li_select_blocks`` builds the sorted index list (text blocks first);
+1. ``li_pool_blocks`` writes the q and k block means (normalised in the same
+   launch for the cosine metric); the tiled copies are never materialised, and
+   with a ``memory.KeyPoolCache`` only the changed key block rows are pooled;
+2. ``li_select_blocks`` builds the sorted index list (text blocks first): a
+   score kernel and a top-k kernel;
 3. ``li_sparse_attn_raster`` reads q, the visual K/V and the text K/V straight
    from the caller's tensors, 3D block by 3D block, and writes the output in
-   q's raster layout.
+   q's raster layout (plus a combine kernel when the last wave's tiles are
+   split).
 
-Three launches, no host synchronisation, no intermediate tiled tensors.
+Five to seven kernel launches, no host synchronisation, no intermediate tiled
+tensors.
 """
 
 from __future__ import annotations
