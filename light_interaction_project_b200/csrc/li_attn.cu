@@ -1,24 +1,33 @@
 // Block-sparse attention forward for sm_100a: TMA + tcgen05 + TMEM.
 //
-// One CTA computes one query block (bs rows, padded to the 128-row MMA tile)
-// of one (b, h) against the key blocks in its index list. Six warps:
-//   warps 0-3  softmax / correction / epilogue — thread t owns query row t,
-//              which is TMEM lane t (warp w reads its lane quarter 32w..32w+31);
-//   warp 4     TMA producer — Q once, then K_j and V_j of every selected block;
-//   warp 5     MMA issuer (one elected lane) + TMEM allocator.
-// TMEM columns: S = Q K^T (fp32, bs columns) at 0, O (fp32, D columns) at 128.
-// The softmax writes P as packed 16-bit pairs over the first bs/2 columns of S,
-// and the PV product reads it from there as the TMEM A operand (TS form), so P
-// never touches shared memory.
+// One CTA per SM computes one query block (bs rows, padded to the 128-row MMA
+// tile) of one (b, h) against the key blocks in its index list. The list is
+// split into two independent online-softmax chains (even and odd positions),
+// so the tensor core works on one chain while the other chain's softmax runs;
+// a single MMA issuer serves both chains in list order, which keeps the two
+// softmaxes taking turns (see the MMA issuer below).
+// Twelve warps (384 threads):
+//   warps 0-3 / 4-7  softmax of chain 0 / 1, then the epilogue — thread t of
+//                    the warpgroup owns query row t, which is TMEM lane t;
+//   warp 8           MMA issuer of both chains (one elected lane) and TMEM
+//                    allocator;
+//   warp 9           TMA producer of Q (once) and of every listed K_j;
+//   warp 10          TMA producer of every listed V_j;
+//   warp 11          no work: it completes the register donor warpgroup.
+// TMEM (all 512 columns): S_0 at 0, S_1 at 128, O_0 at 256, O_1 at 384. The
+// softmax writes P as packed 16-bit pairs over the first bs/2 columns of its
+// chain's S, and the PV product reads it from there as the TMEM A operand (TS
+// form), so P never touches shared memory.
 //
-// Per key block j:  MMA  S = Q K_j^T                -> commit k_empty, s_full
-//                   SM   row max, lazy O rescale, P = exp2(S*c - m) -> p_full
-//                   MMA  O (+)= P V_j                -> commit v_empty, o_full
+// Chain c, block j:  MMA  S_c = Q K_j^T             -> commit k_empty, s_full
+//                    SM   row max, lazy O_c rescale, P = exp2(S*c - m)
+//                    MMA  O_c (+)= P V_j            -> commit v_empty
 // The row max is only moved (and O rescaled) when it grows by more than 8 in
 // log2 units; otherwise the stale max is kept (P <= 2^8), which leaves O/l
-// exact. The producer refills K_{j+1} as soon as S_j completes and V_{j+1} as
-// soon as PV_j completes. Two CTAs share an SM (96 KB smem, 256 TMEM columns
-// each), so one CTA's softmax overlaps the other's MMAs.
+// exact. The K and V producers refill a ring stage as soon as the MMA that read
+// it completes; each walks the block list 32 entries at a time from registers,
+// with the next 32 entries already loading, so no copy waits on an index load.
+// The row arithmetic uses packed f32x2 ops.
 //
 // Operands come straight from the caller's layout through 5-D tensor maps
 // (d, w, h, t, b*h): a 3D (tt, th, tw) block of a raster tensor is one box, and
@@ -42,8 +51,15 @@ namespace li {
 namespace attn {
 
 constexpr int kMaxMaps = 4;
-constexpr int kThreads = 352;  // 8 softmax warps + 2 MMA warps + TMA warp
-constexpr int kWarpMMA0 = 8, kWarpMMA1 = 9, kWarpTMA = 10;
+constexpr int kThreads = 384;  // 8 softmax warps, MMA warp, 2 TMA warps, 1 idle warp
+constexpr int kWarpMMA = 8, kWarpTMAK = 9, kWarpTMAV = 10;  // warp 11: register donor only
+// K and V ring stages (a third stage of either measured no faster).
+constexpr int kRingK = 2, kRingV = 2;
+// Registers per thread: at launch (65536 / 384, rounded down to a multiple of
+// 8), and after the warpgroup split (setmaxnreg). The split never asks for more
+// than the launch holds: 2*128*216 + 128*56 = 62464 <= 384*168 = 64512.
+constexpr int kRegsLaunch = 168, kRegsSoftmax = 216, kRegsIssue = 56;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue <= kThreads * kRegsLaunch, "register split");
 constexpr uint64_t kTimeoutNs = 1000000000ull;  // 1 s per wait
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;  // S_0, S_1 at 0 and 128; O_0, O_1 at 256 and 384
@@ -113,7 +129,7 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait. Returns false when the CTA is aborting (another warp timed
 // out) or this wait ran past kTimeoutNs (then it raises the abort itself).
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                        uint32_t* err, bool honour_abort = true) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = gtimer();
@@ -214,6 +230,31 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed fp32 pair arithmetic (one instruction for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <bool F16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   uint32_t r;
@@ -240,15 +281,19 @@ struct Smem {
   static constexpr int kHalves = D / 64;
   // K and V ring stages: a K stage is refilled once the S MMA that read it has
   // completed, a V stage once its PV MMA has.
-  static constexpr int kNK = 2, kNV = 2;
+  static constexpr int kNK = kRingK, kNV = kRingV;
   static constexpr int kQHalf = 128 * 128;  // 128 rows of 128 bytes
   static constexpr int kKVHalf = BS * 128;
   static constexpr int kKVTile = kHalves * kKVHalf;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kHalves * kQHalf;
   static constexpr int kOffV = kOffK + kNK * kKVTile;
-  static constexpr int kOffX = kOffV + kNV * kKVTile;     // per-row (m, l) of both chains
-  static constexpr int kOffBar = kOffX + 2 * 2 * 128 * 4;
+  // The epilogue's per-row (m, l) of both chains (2 KB) reuses the K ring: it is
+  // written only after every MMA of the tile has completed, so every K load has
+  // landed and been read.
+  static constexpr int kOffX = kOffK;
+  static_assert(kNK * kKVTile >= 2 * 2 * 128 * 4, "K ring holds the epilogue's (m, l)");
+  static constexpr int kOffBar = kOffV + kNV * kKVTile;
   // Barrier area: q | k_full[kNK] k_empty[kNK] | v_full[kNV] v_empty[kNV] |
   // s_full[2] | o_full[2] | xs | st, then the TMEM base address and the abort flag.
   static constexpr int kBarKF = 8, kBarKE = kBarKF + 8 * kNK, kBarVF = kBarKE + 8 * kNK;
@@ -256,6 +301,7 @@ struct Smem {
   static constexpr int kBarXS = kBarO + 16, kBarST = kBarXS + 8, kSlot = kBarST + 8, kAbort = kSlot + 4;
   static_assert(kAbort + 4 <= 256, "barrier area");
   static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
+  static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
   static constexpr uint32_t kTileBytes = (uint32_t)kKVTile;
 };
 
@@ -271,11 +317,69 @@ __device__ __forceinline__ void block_coords(int raster, int blk, int bsz, int n
   c[4] = w;
 }
 
-// Named barrier over one chain's 4 softmax warps and its MMA warp. Every
+// Named barrier over one chain's 4 softmax warps and the MMA warp. Every
 // participant executes it exactly once per block of the chain (work is
 // skipped, never the barrier, after an abort), so counts always match.
 __device__ __forceinline__ void chain_sync(int chain) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + chain), "r"(160) : "memory");
+}
+
+// One TMA producer warp: loads tile j of every listed block into a ring of NST
+// stages (full barrier full0 + 8*stage, empty barrier empty0 + 8*stage). The
+// whole warp walks the list: lane l holds entry base + l of the current 32
+// entries, and the next 32 are already loading, so an index load never stands
+// between two copies; lane 0 waits for the stage and issues the copy. After an
+// abort, lane 0 drains the copies it issued (and, for the K producer, Q's)
+// before the CTA's shared memory is released.
+template <int NST, int BS>
+__device__ __forceinline__ void produce(const Params& p, const int32_t* irow, int S, int lane, int wc, int mi,
+                                        uint32_t ring, uint32_t tile_bytes, uint32_t half_bytes, int halves,
+                                        uint32_t full0, uint32_t empty0, const CUtensorMap* vis_maps,
+                                        const CUtensorMap* txt_maps, volatile int* abort_flag, uint32_t bar_q) {
+  int32_t cur = lane < S ? irow[(int64_t)lane * p.i_s] : 0;
+  int32_t nxt = 32 + lane < S ? irow[(int64_t)(32 + lane) * p.i_s] : 0;
+  int issued = 0;
+  for (int j = 0; j < S; ++j) {
+    if (j > 0 && (j & 31) == 0) {
+      cur = nxt;
+      nxt = j + 32 + lane < S ? irow[(int64_t)(j + 32 + lane) * p.i_s] : 0;
+    }
+    int blk = __shfl_sync(0xFFFFFFFFu, cur, j & 31);
+    int ok = 1;
+    if (lane == 0) {
+      if (blk < 0 || blk >= p.n_kv) {
+        if (p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
+        blk = 0;
+      }
+      int c[5];
+      const CUtensorMap* m;
+      if (p.kv_raster && blk < p.ntxt) {
+        block_coords(0, blk, BS, 1, 1, 1, 1, 1, wc, c);
+        m = &txt_maps[mi];
+      } else {
+        block_coords(p.kv_raster, p.kv_raster ? blk - p.ntxt : blk, BS, p.k_nh, p.k_nw, p.k_tt,
+                     p.k_th, p.k_tw, wc, c);
+        m = &vis_maps[mi];
+      }
+      const int st = j % NST;
+      if (j >= NST && !mbar_wait(empty0 + 8 * st, ((j / NST) - 1) & 1, abort_flag, p.err)) {
+        ok = 0;
+      } else {
+        mbar_expect_tx(full0 + 8 * st, tile_bytes);
+        for (int hf = 0; hf < halves; ++hf) {
+          c[0] = 64 * hf;
+          tma_load_5d(ring + st * tile_bytes + hf * half_bytes, m, c, full0 + 8 * st);
+        }
+        issued = j + 1;
+      }
+    }
+    if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+  }
+  if (lane == 0 && *abort_flag) {
+    if (bar_q) mbar_wait(bar_q, 0, abort_flag, nullptr, false);
+    for (int j = issued - NST; j < issued; ++j)
+      if (j >= 0) mbar_wait(full0 + 8 * (j % NST), (j / NST) & 1, abort_flag, nullptr, false);
+  }
 }
 
 template <int D, int BS, bool F16>
@@ -332,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kWarpMMA0) tmem_alloc(smem_u32(smem + L::kOffBar + L::kSlot), kTmemCols);
+  if (warp == kWarpMMA) tmem_alloc(smem_u32(smem + L::kOffBar + L::kSlot), kTmemCols);
   if (BS < 128 && warp < 4) {
     // Query rows past the block are zero so the padded MMA rows stay finite.
     for (int hf = 0; hf < L::kHalves; ++hf) {
@@ -345,116 +449,96 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == kWarpTMA) {
-    // ------------------------------ producer ------------------------------
-    if (lane == 0 && S > 0) {
-      int c[5];
-      block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
-      mbar_expect_tx(bar_q, L::kTileBytes);
-      for (int hf = 0; hf < L::kHalves; ++hf) {
-        c[0] = 64 * hf;
-        tma_load_5d(sb + L::kOffQ + hf * L::kQHalf, &p.q_map[mi], c, bar_q);
-      }
-      int issued_k = 0, issued_v = 0;
-      int nxt = irow[0];
-      for (int j = 0; j < S; ++j) {
-        int blk = nxt;
-        if (j + 1 < S) nxt = irow[(int64_t)(j + 1) * p.i_s];
-        if (blk < 0 || blk >= p.n_kv) {
-          if (p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
-          blk = 0;
-        }
-        const CUtensorMap* km;
-        const CUtensorMap* vm;
-        if (p.kv_raster && blk < p.ntxt) {
-          block_coords(0, blk, BS, 1, 1, 1, 1, 1, wc, c);
-          km = &p.kt_map[mi]; vm = &p.vt_map[mi];
-        } else {
-          block_coords(p.kv_raster, p.kv_raster ? blk - p.ntxt : blk, BS, p.k_nh, p.k_nw, p.k_tt, p.k_th, p.k_tw,
-                       wc, c);
-          km = &p.k_map[mi]; vm = &p.v_map[mi];
-        }
-        const int ks = j % L::kNK, vs = j % L::kNV;
-        if (j >= L::kNK && !mbar_wait(bar_ke(ks), ((j / L::kNK) - 1) & 1, abort_flag, p.err)) break;
-        mbar_expect_tx(bar_kf(ks), L::kTileBytes);
+  // Register split: the launch gives every thread kRegsLaunch; the MMA/TMA
+  // warpgroup (warps 8-11) hands most of its share to the two softmax
+  // warpgroups. 2 * 128 * kRegsSoftmax + 128 * kRegsIssue <= 384 * kRegsLaunch.
+  if (warp >= kWarpMMA) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsIssue));
+  if (warp == kWarpTMAK || warp == kWarpTMAV) {
+    // ------------------------------ producers ------------------------------
+    if (S > 0) {
+      if (warp == kWarpTMAK && lane == 0) {
+        int c[5];
+        block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+        mbar_expect_tx(bar_q, L::kTileBytes);
         for (int hf = 0; hf < L::kHalves; ++hf) {
           c[0] = 64 * hf;
-          tma_load_5d(sb + L::kOffK + ks * L::kKVTile + hf * L::kKVHalf, km, c, bar_kf(ks));
+          tma_load_5d(sb + L::kOffQ + hf * L::kQHalf, &p.q_map[mi], c, bar_q);
         }
-        issued_k = j + 1;
-        if (j >= L::kNV && !mbar_wait(bar_ve(vs), ((j / L::kNV) - 1) & 1, abort_flag, p.err)) break;
-        mbar_expect_tx(bar_vf(vs), L::kTileBytes);
-        for (int hf = 0; hf < L::kHalves; ++hf) {
-          c[0] = 64 * hf;
-          tma_load_5d(sb + L::kOffV + vs * L::kKVTile + hf * L::kKVHalf, vm, c, bar_vf(vs));
-        }
-        issued_v = j + 1;
       }
-      if (*abort_flag) {
-        // Drain this CTA's own loads before shared memory is released.
-        mbar_wait(bar_q, 0, abort_flag, nullptr, false);
-        for (int j = issued_k - L::kNK; j < issued_k; ++j)
-          if (j >= 0) mbar_wait(bar_kf(j % L::kNK), (j / L::kNK) & 1, abort_flag, nullptr, false);
-        for (int j = issued_v - L::kNV; j < issued_v; ++j)
-          if (j >= 0) mbar_wait(bar_vf(j % L::kNV), (j / L::kNV) & 1, abort_flag, nullptr, false);
-      }
+      if (warp == kWarpTMAK)
+        produce<L::kNK, BS>(p, irow, S, lane, wc, mi, sb + L::kOffK, L::kKVTile, L::kKVHalf, L::kHalves, bar0 + L::kBarKF,
+                        bar0 + L::kBarKE, p.k_map, p.kt_map, abort_flag, bar_q);
+      else
+        produce<L::kNV, BS>(p, irow, S, lane, wc, mi, sb + L::kOffV, L::kKVTile, L::kKVHalf, L::kHalves, bar0 + L::kBarVF,
+                        bar0 + L::kBarVE, p.v_map, p.vt_map, abort_flag, 0);
     }
-  } else if (warp == kWarpMMA0 || warp == kWarpMMA1) {
-    // --------------------- MMA issuer of chain w ----------------------------
-    // Chain w owns key blocks j = w, w+2, ...: S_j = Q K_j^T into TMEM S_w, then
-    // (after the chain's softmax) O_w += P_j V_j. One lane issues; MMAs of one
-    // thread run in order, so S_{j+2} (issued after PV_j) never overwrites P_j
-    // before PV_j has read it, and s_full for S_j also covers PV_{j-2}.
-    const int w = warp - kWarpMMA0;
-    const int nb = n_chain[w];
+  } else if (warp == kWarpMMA) {
+    // ------------------ MMA issuer of both chains (one lane) ------------------
+    // Chain c owns key blocks j = c, c+2, ...: S_j = Q K_j^T into TMEM S_c, then
+    // (after chain c's softmax) O_c += P_j V_j. One thread issues every MMA, in
+    // the order S_0, S_1, PV_0, S_2, PV_1, S_3, ...; MMAs of one thread run in
+    // order, so the tensor core works on one chain while the other chain's
+    // softmax runs and the two softmaxes take turns on the MUFU unit (two
+    // independent issuers drift into lockstep, where both softmaxes run at once
+    // and the tensor core idles meanwhile). S_{j+2}, issued after PV_j, never
+    // overwrites P_j before PV_j has read it, and s_full of S_j also covers
+    // PV_{j-2}.
     constexpr uint32_t idS = idesc_f16(128, BS, F16, false);
     constexpr uint32_t idPV = idesc_f16(128, D, F16, true);
-    const uint32_t tS = tmem + kColS + (uint32_t)w * 128, tO = tmem + kColO + (uint32_t)w * 128;
+    const uint64_t qd = sdesc(sb + L::kOffQ, 16, 1024);
+    const uint64_t kd0 = sdesc(sb + L::kOffK, 16, 1024);
+    const uint64_t vd0 = sdesc(sb + L::kOffV, L::kKVHalf, 1024);
     auto issue_s = [&](int j) {
       const int ks = j % L::kNK;
       if (!mbar_wait(bar_kf(ks), (j / L::kNK) & 1, abort_flag, p.err)) return;
       tc_fence_after();
-      const uint32_t kbase = sb + L::kOffK + ks * L::kKVTile;
+      const uint64_t kd = kd0 + (uint64_t)((ks * L::kKVTile) >> 4);
+      const uint32_t tS = tmem + kColS + (uint32_t)(j & 1) * 128;
+      // A K-step moves 32 bytes along a 128-byte swizzled row, four steps per
+      // 64-column half: the descriptors differ only in their start address
+      // field (address >> 4, no carry: shared addresses stay below 2^18).
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint64_t ad = sdesc(sb + L::kOffQ + (kk >> 2) * L::kQHalf + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = sdesc(kbase + (kk >> 2) * L::kKVHalf + (kk & 3) * 32, 16, 1024);
-        mma_ss(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
-      }
+      for (int kk = 0; kk < D / 16; ++kk)
+        mma_ss(tS, qd + (uint64_t)(((kk >> 2) * L::kQHalf + (kk & 3) * 32) >> 4),
+               kd + (uint64_t)(((kk >> 2) * L::kKVHalf + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
       mma_commit(bar_ke(ks));
-      mma_commit(bar_s(w));
+      mma_commit(bar_s(j & 1));
     };
-    if (lane == 0 && nb > 0 && mbar_wait(bar_q, 0, abort_flag, p.err)) {
+    if (lane == 0 && S > 0 && mbar_wait(bar_q, 0, abort_flag, p.err)) {
       tc_fence_after();
-      issue_s(w);
+      issue_s(0);
+      if (S > 1) issue_s(1);
     }
-    for (int i = 0; i < nb; ++i) {
-      const int j = w + 2 * i;
-      chain_sync(w);  // softmax of block j has written P_j (or skipped after an abort)
+    for (int j = 0; j < S; ++j) {
+      const int c = j & 1;
+      chain_sync(c);  // chain c's softmax has written P_j (or skipped after an abort)
       if (lane == 0 && !*abort_flag) {
         tc_fence_after();
         const int vs = j % L::kNV;
         if (mbar_wait(bar_vf(vs), (j / L::kNV) & 1, abort_flag, p.err)) {
           tc_fence_after();
-          const uint32_t vbase = sb + L::kOffV + vs * L::kKVTile;
+          const uint64_t vd = vd0 + (uint64_t)((vs * L::kKVTile) >> 4);
+          const uint32_t tS = tmem + kColS + (uint32_t)c * 128, tO = tmem + kColO + (uint32_t)c * 128;
 #pragma unroll
-          for (int kk = 0; kk < BS / 16; ++kk) {
-            const uint64_t bd = sdesc(vbase + kk * 2048, L::kKVHalf, 1024);
-            mma_ts(tO, tS + kk * 8, bd, idPV, (i > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < BS / 16; ++kk)
+            mma_ts(tO, tS + kk * 8, vd + (uint64_t)((kk * 2048) >> 4), idPV, (j >= 2 || kk > 0) ? 1u : 0u);
           mma_commit(bar_ve(vs));
-          if (i + 1 < nb) issue_s(j + 2);
+          if (j + 2 < S) issue_s(j + 2);
         }
       }
       __syncwarp();
     }
-    if (lane == 0 && nb > 0) {
-      // Every MMA of this chain completes before O_w is read and TMEM is freed.
-      mma_commit(bar_o(w));
-      mbar_wait(bar_o(w), 0, abort_flag, p.err, false);
+    if (lane == 0 && S > 0) {
+      // Every MMA completes before O is read and TMEM is freed.
+      for (int c = 0; c < 2; ++c)
+        if (n_chain[c] > 0) mma_commit(bar_o(c));
+      for (int c = 0; c < 2; ++c)
+        if (n_chain[c] > 0) mbar_wait(bar_o(c), 0, abort_flag, p.err, false);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // --------------------- softmax of chain w + epilogue -----------------------
     // Thread (warp, lane) owns row = (warp & 3) * 32 + lane = TMEM lane.
     const int w = warp >> 2;
@@ -474,43 +558,40 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 #pragma unroll
         for (int cc = 0; cc < BS / 32; ++cc) tmem_ld32(tS + cc * 32, r[cc]);
         tmem_wait_ld();
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int cc = 0; cc < BS / 32; ++cc)
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            mx0 = fmaxf(mx0, __uint_as_float(r[cc][e]));
-            mx1 = fmaxf(mx1, __uint_as_float(r[cc][e + 1]));
-            mx2 = fmaxf(mx2, __uint_as_float(r[cc][e + 2]));
-            mx3 = fmaxf(mx3, __uint_as_float(r[cc][e + 3]));
-          }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+          for (int e = 0; e < 32; e += 8)
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+              mxa[a] = fmax3(mxa[a], __uint_as_float(r[cc][e + 2 * a]), __uint_as_float(r[cc][e + 2 * a + 1]));
+        const float mx = fmaxf(fmax3(mxa[0], mxa[1], mxa[2]), mxa[3]);
         const float m_new = fmaxf(m, mx * c2);
         // Lazy correction: move the reference max only when it grows by more
         // than 8 (log2 units); P <= 2^8 otherwise, and O/l stays exact.
         const bool need = (i > 0) && (m_new - m > 8.0f);
         const float alpha = need ? ex2(m - m_new) : 1.f;
         if (i == 0 || need) m = m_new;
-        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        // p = 2^(s*c - m) for column pairs; P goes back over S as packed
+        // 16-bit pairs.
+        const float2 c2v = make_float2(c2, c2), nm = make_float2(-m, -m);
+        float2 la = make_float2(0.f, 0.f), lb = make_float2(0.f, 0.f);
 #pragma unroll
         for (int cc = 0; cc < BS / 32; ++cc) {
           uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(r[cc][2 * e]), c2, -m));
-            const float p1 = ex2(fmaf(__uint_as_float(r[cc][2 * e + 1]), c2, -m));
-            const float p2 = ex2(fmaf(__uint_as_float(r[cc][2 * e + 2]), c2, -m));
-            const float p3 = ex2(fmaf(__uint_as_float(r[cc][2 * e + 3]), c2, -m));
-            l0 += p0;
-            l1 += p1;
-            l2 += p2;
-            l3 += p3;
-            pk[e] = pack2<F16>(p0, p1);
-            pk[e + 1] = pack2<F16>(p2, p3);
+          for (int e2 = 0; e2 < 16; ++e2) {
+            const float2 x =
+                ffma2(make_float2(__uint_as_float(r[cc][2 * e2]), __uint_as_float(r[cc][2 * e2 + 1])), c2v, nm);
+            const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+            if (e2 & 1) lb = fadd2(lb, pp);
+            else la = fadd2(la, pp);
+            pk[e2] = pack2<F16>(pp.x, pp.y);
           }
           tmem_st16(tS + cc * 16, pk);
         }
-        l = l * alpha + ((l0 + l1) + (l2 + l3));
+        l = l * alpha + ((la.x + la.y) + (lb.x + lb.y));
         // O_w rescale (its last PV completed before s_full of this block fired;
         // PV_j is only issued after the chain barrier below).
         if (__any_sync(0xFFFFFFFFu, need)) {
@@ -530,14 +611,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       chain_sync(w);  // P_j is in TMEM: the chain's MMA warp may issue PV_j
     }
     // ---- epilogue: merge the two chains, O = (a0 O_0 + a1 O_1) / (a0 l0 + a1 l1)
-    if (ok && nb > 0) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o(w), 0, abort_flag, p.err));
-    xm[w * 128 + row] = m;
-    xl[w * 128 + row] = l;
+    // Every MMA of both chains completes first: (m, l) go to the K ring, which
+    // is free once the last S MMA has read its stage.
+    for (int c = 0; c < 2; ++c)
+      if (ok && n_chain[c] > 0) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o(c), 0, abort_flag, p.err));
+    if (ok) {
+      xm[w * 128 + row] = m;
+      xl[w * 128 + row] = l;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(bar_xs);
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_xs, 0, abort_flag, p.err));
-    if (ok && n_chain[1 - w] > 0)
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_o(1 - w), 0, abort_flag, p.err));
     tc_fence_after();
     const float m0 = xm[row], m1 = xm[128 + row], l0 = xl[row], l1 = xl[128 + row];
     const float mm = fmaxf(m0, m1);
@@ -626,7 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMMA0) {
+  if (warp == kWarpMMA) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
