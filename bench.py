@@ -233,6 +233,34 @@ def workload_config(cfg, args, world):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def exchange_check(stack, x, group):
+    """Layer 0's two exchanges through the NVLink peer path (li_a2a_push) and through
+    NCCL all_to_all_single on the same inputs; True when every rank's receive buffers
+    agree bit for bit (one collective vote)."""
+    from light_interaction_project_b200.ulysses import head_to_seq
+    cfg, world, rank, hl = stack.cfg, stack.world, stack.rank, stack.hl
+    B, s, _ = x.shape
+    D = cfg.head_dim
+    send = torch.matmul(x.reshape(B * s, cfg.hidden), stack.w_qkv_rank[0])          # [P, s, 3*hl*D]
+    row = 3 * hl * D * send.element_size()
+    got = stack.ex_qkv.push(send, s, row, s * row, row, rank * s * row, row)[: world * s * 3 * hl * D].clone()
+    want = torch.empty_like(send)
+    dist.all_to_all_single(want, send, group=group)
+    ok = torch.equal(got.view_as(want), want)
+    g = torch.Generator(device=x.device)
+    g.manual_seed(99 + rank)
+    o_tok = torch.randn(B, world * s, hl, D, generator=g, device=x.device).to(torch.bfloat16)
+    row = hl * D * o_tok.element_size()
+    got = stack.ex_out.push(o_tok, s, row, s * row, row, rank * row, cfg.heads * row // hl)
+    got = got[: s * cfg.heads * D].view(B, s, cfg.heads, D).clone()
+    want = head_to_seq(o_tok.permute(0, 2, 1, 3), world, group)
+    ok = ok and torch.equal(got, want)
+    vote = torch.tensor([1 if ok else 0], device=x.device, dtype=torch.int32)
+    dist.all_reduce(vote, op=dist.ReduceOp.MIN, group=group)
+    torch.cuda.synchronize()
+    return bool(vote.item())
+
+
 def run_gpu(args, cfg, rank, world, local_rank):
     from light_interaction_project_b200 import _lib as L
     from light_interaction_project_b200 import kernels as K
@@ -259,6 +287,17 @@ def run_gpu(args, cfg, rank, world, local_rank):
     group = dist.group.WORLD if world > 1 else None
     stack = HeadShardedStack(cfg, rank, world, dev, group=group)
     x0 = stack.make_input()
+    # N > 1 with the peer exchange: check it bit for bit against NCCL on this box
+    # before anything is timed; on a mismatch every rank falls back to NCCL.
+    exch = None
+    if world > 1:
+        exch = {"transport": cfg.exchange, "check": None}
+        if stack.ex_qkv is not None:
+            ok = exchange_check(stack, x0, group)
+            exch["check"] = ok
+            if not ok:
+                stack.close()
+                exch["transport"] = "nccl (peer exchange failed its check)"
 
     def barrier():
         if world > 1:
@@ -305,23 +344,33 @@ def run_gpu(args, cfg, rank, world, local_rank):
         attn_timing["on"] = False
         barrier()
     attn_ms = [a.elapsed_time(b) for a, b in attn_timing["events"]]
-    # End-to-end: host input -> device, step, device output -> host.
+    # End-to-end: host input -> device, step, device output -> host, all on the
+    # step's stream; the copies also get their own events.
     x_host = x0.cpu().pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
     barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    copy_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     s2.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        ev = copy_ev[i]
+        ev[0].record()
         if args.graph:
             x0.copy_(x_host, non_blocking=True)
+            ev[1].record()
             y = stack.replay()
         else:
             xd = x_host.to(dev, non_blocking=True)
+            ev[1].record()
             y = stack.step(xd)
+        ev[2].record()
         y_host.copy_(y, non_blocking=True)
+        ev[3].record()
     e2.record()
     barrier()
     ms_e2e = s2.elapsed_time(e2)
+    h2d_ms = sum(ev[0].elapsed_time(ev[1]) for ev in copy_ev) / args.steps
+    d2h_ms = sum(ev[2].elapsed_time(ev[3]) for ev in copy_ev) / args.steps
     K.raise_device_errors(dev)
 
     if world > 1:
@@ -336,10 +385,10 @@ def run_gpu(args, cfg, rank, world, local_rank):
         torch.set_num_threads(os.cpu_count() or 1)
         cpu = cpu_reference_sample(cfg)
         torch.set_num_threads(prev)
-    t = torch.tensor([ms, ms_e2e, sum(attn_ms) / len(attn_ms)], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms, ms_e2e, sum(attn_ms) / len(attn_ms), h2d_ms, d2h_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, attn_call_ms = t.tolist()
+    ms, ms_e2e, attn_call_ms, h2d_ms, d2h_ms = t.tolist()
     if rank != 0:
         return
     total_flops = cfg.attention_flops() * cfg.layers * args.steps
@@ -361,12 +410,16 @@ def run_gpu(args, cfg, rank, world, local_rank):
                      "frac": achieved / sustained, "traffic": traffic,
                      "peak_kind": f"{kind} bf16 sustained (burst {burst})",
                      "traffic_source": tfile},
-        "e2e": {"value": e2e_value, "unit": UNIT,
+        "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": ms_e2e / args.steps,
                 "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size() * world),
-                "d2h_bytes_per_step": int(y_host.numel() * y_host.element_size() * world)},
+                "d2h_bytes_per_step": int(y_host.numel() * y_host.element_size() * world),
+                "h2d_ms_per_step": h2d_ms, "d2h_ms_per_step": d2h_ms},
         "gpu_launches": int(n_launch * world),
         "clocks": clk.summary(),
     }
+    if exch is not None:
+        line["exchange_check"] = exch["check"]
+        line["config"]["exchange"] = exch["transport"]
     if cpu is not None:
         cpu_s, cpu_fl, threads = cpu
         line["cpu_baseline"] = {"value": cpu_fl / cpu_s / 1e12, "unit": UNIT, "cores": threads, "kind": "port",

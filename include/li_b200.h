@@ -296,6 +296,9 @@ typedef struct li_a2a_desc {
  * once every rank's chunk for this rank has landed. Every rank must make the
  * same sequence of calls; one descriptor's counter serves one stream. A peer
  * that does not join within 2 s sets LI_DEVERR_TIMEOUT and the kernel returns.
+ * After LI_DEVERR_TIMEOUT the exchange's buffers must not be used again: a
+ * late peer may still be writing into them while the epoch has moved on, so
+ * the caller frees them and builds a new exchange (new buffers, new flags).
  * With `epoch_word` set (a zeroed u32 on this rank's device) the call's epoch is
  * *epoch_word + 1, read and stored back by the kernel, and `epoch` is ignored:
  * the launch then carries no per-call value, so a captured CUDA graph can replay

@@ -58,6 +58,9 @@ def run_sparse_attention(q, k_txt, v_txt, k_vis, v_vis, block_idx, latent_hw, sp
     q ``[B, H, Nq, D]``, text K/V ``[B, H, N_txt, D]``, visual K/V ``[B, H, N_vis, D]``
     (any strides with D contiguous). Falls back to dense attention, as the
     reference does, when the query length is not a whole number of latent frames.
+    Device-side errors (a bounded wait that gave up; a block id out of range)
+    do not raise here: the kernels record them in the device error word, which
+    ``kernels.raise_device_errors()`` reads (and synchronises) at a step boundary.
     """
     LH, LW = latent_hw
     if q.shape[2] % (LH * LW) != 0:

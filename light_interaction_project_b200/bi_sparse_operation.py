@@ -53,6 +53,9 @@ def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params,
     output projection reads it without a re-layout copy.
     ``k_pool`` (extension): a ``memory.KeyPoolCache`` refreshed by the caller for
     this ``k``'s visual part; the key pooling is then skipped.
+    Device-side errors (a bounded wait that gave up; a block id out of range)
+    do not raise here: the kernels record them in the device error word, which
+    ``kernels.raise_device_errors()`` reads (and synchronises) at a step boundary.
     """
     LH, LW = latent_hw
     if q.shape[2] % (LH * LW) != 0:

@@ -65,7 +65,11 @@ def generate_prefill_indices(q_in, k_in, text_len, grid_thw, params, device, q_b
 def run_sparse_prefill_attention(q, k_txt, v_txt, k_vis, v_vis, block_idx, latent_hw, sparse_params):
     """One bidirectional (prefill) sparse-attention forward —
     ``bi_sparse_operation_for_KV_cache.py:301-395``. Dense for the first three
-    chunks (``current_chunk_index < 3``) and for untileable query lengths."""
+    chunks (``current_chunk_index < 3``) and for untileable query lengths.
+    Device-side errors (a bounded wait that gave up; a block id out of range)
+    do not raise here: the kernels record them in the device error word, which
+    ``kernels.raise_device_errors()`` reads (and synchronises) at a step boundary.
+    """
     current = getattr(get_infer_state(), "current_chunk_index", 0)
     LH, LW = latent_hw
     if current < 3 or q.shape[2] % (LH * LW) != 0:

@@ -644,6 +644,9 @@ li_status prepare_select(const li_view4* q_pool, const li_view4* k_pool, const l
   const int64_t Nq = q_pool->shape[2], D = q_pool->shape[3];
   const int64_t Nk = k_pool->shape[2];
   const int dt = q_pool->dtype;
+  if (B < 0 || H < 0 || Nq < 0 || Nk < 0)
+    return fail(LI_ERR_SHAPE, "pool shapes must be non-negative (B=%lld H=%lld Nq=%lld Nk=%lld)", (long long)B,
+                (long long)H, (long long)Nq, (long long)Nk);
   if (!valid_dtype(dt) || k_pool->dtype != dt) return fail(LI_ERR_INVALID_ARG, "pool dtypes must match");
   if (k_pool->shape[0] != B || k_pool->shape[1] != H || k_pool->shape[3] != D)
     return fail(LI_ERR_SHAPE, "k_pool shape does not match q_pool");
@@ -706,7 +709,15 @@ li_status prepare_select(const li_view4* q_pool, const li_view4* k_pool, const l
   return LI_OK;
 }
 
-int64_t select_ws_bytes(int64_t B, int64_t H, int64_t Nq, int64_t Nk) { return B * H * Nq * Nk * 4; }
+// Key scratch of the two-kernel path: B*H*Nq*Nk 32-bit keys. Saturates at
+// INT64_MAX instead of overflowing (no caller can hold that much).
+int64_t select_ws_bytes(int64_t B, int64_t H, int64_t Nq, int64_t Nk) {
+  int64_t n = 4;
+  for (int64_t f : {B, H, Nq, Nk}) {
+    if (f < 0 || __builtin_mul_overflow(n, f, &n)) return INT64_MAX;
+  }
+  return n;
+}
 
 // Shared memory of topk_kernel: four warps' 256-bin histograms and key rows.
 size_t topk_smem(int64_t Nk) { return (size_t)4 * 256 * 4 + (size_t)16 * Nk; }
@@ -766,6 +777,7 @@ li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStrea
 extern "C" li_status li_select_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks, int64_t n_k_blocks,
                                                int64_t* bytes) {
   if (!bytes) return fail(LI_ERR_INVALID_ARG, "bytes is required");
+  if (batch < 0 || heads < 0 || n_q_blocks < 0 || n_k_blocks < 0) return fail(LI_ERR_SHAPE, "negative shape");
   *bytes = topk_smem(n_k_blocks) <= kSmemBudget ? select_ws_bytes(batch, heads, n_q_blocks, n_k_blocks) : 0;
   return LI_OK;
 }

@@ -30,7 +30,11 @@ def longcat_flash_attn(q, k, v, block_indices, block_counts, sm_scale=None, logi
 
     ``validate=False`` skips the host-side index bound check (which, as in the
     reference, reads ``block_indices.max()`` and so synchronises); the kernel
-    still guards every index on the device.
+    still guards every index on the device, but asynchronously: an out-of-range
+    block id is read as block 0 and sets ``LI_DEVERR_BAD_INDEX`` in the device
+    error word, and this call returns normally. ``kernels.raise_device_errors()``
+    (a synchronising read, e.g. at a step boundary) turns that into the
+    reference's ``ValueError``.
     """
     B, H, Q_len, D = q.shape
     K_len = k.shape[2]

@@ -88,6 +88,11 @@ class PeerExchange:
     into rank p's receive buffer and returns, on the current stream, once this
     rank's receive buffer is complete. Every rank must make the same calls in the
     same order; one exchange serves one stream.
+
+    A peer that does not arrive within 2 s makes the call set
+    ``LI_DEVERR_TIMEOUT`` in the device error word and return. After that the
+    exchange must not be used again (a late peer may still write into the
+    receive buffers): :meth:`close` it and build a new one.
     """
 
     def __init__(self, recv_bytes: int, rank: int, world: int, device, group=None):
@@ -194,7 +199,9 @@ class StackConfig:
     batch: int = 1
     # N > 1: "nccl" (all_to_all_single) or "peer" (li_a2a_push over NVLink peer memory,
     # bit-identical; with the step captured as one CUDA graph the faster of the two:
-    # 15.84 vs 16.06 ms per 30-layer step at 8 GPUs)
+    # 15.84 vs 16.06 ms per 30-layer step at 8 GPUs). The library default stays NCCL,
+    # which needs no CUDA-IPC mappings; bench.py selects "peer" only after checking
+    # it bit for bit against NCCL on the same box (its "exchange_check").
     exchange: str = "nccl"
 
     @property
@@ -349,9 +356,15 @@ class HeadShardedStack:
                 ex.close()
         self.ex_qkv = self.ex_out = None
 
-    def step(self, x: torch.Tensor, attn_events=None) -> torch.Tensor:
+    def step(self, x: torch.Tensor, attn_events=None, check_errors: bool = False) -> torch.Tensor:
+        """One step of every layer. ``check_errors``: synchronise afterwards and raise if
+        a kernel reported a device-side error (a bad block id, a bounded wait that
+        gave up); device errors are otherwise only visible through
+        ``kernels.raise_device_errors``."""
         for i in range(self.cfg.layers):
             x = self.layer(i, x, attn_events[i] if attn_events is not None else None)
+        if check_errors:
+            K.raise_device_errors(self.device)
         return x
 
     def capture(self, x: torch.Tensor, warmup: int = 2) -> torch.Tensor:
@@ -389,11 +402,14 @@ class HeadShardedStack:
         self._graph = (graph, y)
         return y
 
-    def replay(self) -> torch.Tensor:
-        """Runs the captured step on the current contents of its static input."""
+    def replay(self, check_errors: bool = False) -> torch.Tensor:
+        """Runs the captured step on the current contents of its static input
+        (``check_errors`` as in :meth:`step`)."""
         if self._graph is None:
             raise RuntimeError("HeadShardedStack.capture() has not been called")
         self._graph[0].replay()
+        if check_errors:
+            K.raise_device_errors(self.device)
         return self._graph[1]
 
     def release_graph(self):

@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference checkout is readable:
 
-    python tests/golden/make_golden.py [--ref-root PATH]
+    python tests/golden/make_golden.py --ref-root PATH   (or LI_REFERENCE_ROOT=PATH)
 
 It imports the reference's sparse-attention modules unchanged (a small package
 shim satisfies their relative imports; ``hyvideo.commons.infer_state`` is
@@ -349,9 +349,12 @@ CASES = {
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default=os.environ.get("LI_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref-root", default=os.environ.get("LI_REFERENCE_ROOT"),
+                    help="root of the reference checkout (required; or set LI_REFERENCE_ROOT)")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
+    if not args.ref_root:
+        ap.error("--ref-root (or LI_REFERENCE_ROOT) must name the reference checkout")
     torch.manual_seed(0)
     mods, state = _load_reference(args.ref_root)
     for name, fn in CASES.items():

@@ -83,6 +83,28 @@ def test_entry_points_validate_before_launch(lib):
         L.check(st, "attn")
 
 
+def test_selection_scratch_sizes_never_overflow(lib):
+    """The selection's key-scratch size saturates instead of wrapping, negative
+    shapes are refused, and the no-allocation entry point refuses a negative pool
+    shape before touching the device."""
+    nbytes = ctypes.c_int64()
+    assert lib.li_select_workspace_bytes(1, 24, 56, 952, ctypes.byref(nbytes)) == L.LI_OK
+    assert nbytes.value == 24 * 56 * 952 * 4
+    assert lib.li_select_workspace_bytes(1 << 40, 1 << 40, 1, 1, ctypes.byref(nbytes)) == L.LI_OK
+    assert nbytes.value == 2 ** 63 - 1
+    assert lib.li_select_workspace_bytes(-1, 24, 56, 952, ctypes.byref(nbytes)) == L.LI_ERR_SHAPE
+    q = L.View4()
+    q.data = 256
+    for i, (sh, st) in enumerate(zip((-1, 1, 4, 128), (512, 512, 128, 1))):
+        q.shape[i], q.stride[i] = sh, st
+    q.dtype = L.DTYPE_BF16
+    p = K.select_params(L.SELECT_DECODE, "dot", (1, 8, 16), (1, 2, 2), (1, 2, 2), 0, 0, 1.0)
+    iv = L.IndexView()
+    st = lib.li_select_blocks_static(ctypes.byref(q), ctypes.byref(q), ctypes.byref(p), None, ctypes.byref(iv),
+                                     None, None)
+    assert st == L.LI_ERR_SHAPE and "non-negative" in L.last_error()
+
+
 def test_split_plan_workspace(lib):
     """Tail split: only the tiles of a mostly idle last wave (148 SMs, one CTA
     each) are cut into list pieces; the workspace holds exactly their partials."""

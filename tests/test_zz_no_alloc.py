@@ -74,10 +74,15 @@ def test_static_scratch_matches_workspace_path(cuda_ok, case):
         _call_workspace(lib, qp, kp, p, bias, *want)
         got = _outputs(B, H, nq, ntxt + kb, nk, dev)
         torch.cuda.synchronize()
+        allocs_before = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
         free_before = torch.cuda.mem_get_info(dev)[0]
         L.check(_call_static(lib, qp, kp, p, bias, *got), "li_select_blocks_static")
         torch.cuda.synchronize()
-        if call:  # after the first call's one-time lookup, a call reserves no device memory
+        # No allocation through torch's allocator, and (a device-wide hint, since
+        # another process could allocate meanwhile) no device memory reserved
+        # after the first call's one-time address lookup.
+        assert torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0) == allocs_before
+        if call:
             assert torch.cuda.mem_get_info(dev)[0] == free_before
         assert torch.equal(got[0], want[0]), f"indices differ on call {call}"
         assert torch.equal(got[1], want[1]), f"counts differ on call {call}"
