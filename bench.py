@@ -234,27 +234,29 @@ def workload_config(cfg, args, world):
 # GPU arm
 # ---------------------------------------------------------------------------
 def exchange_check(stack, x, group):
-    """Layer 0's two exchanges through the NVLink peer path (li_a2a_push) and through
-    NCCL all_to_all_single on the same inputs; True when every rank's receive buffers
-    agree bit for bit (one collective vote)."""
+    """Layer 0's two exchanges through the NVLink peer path (li_a2a_push: q into the
+    receive buffer, k and v into the owners' resident K/V buffers; the output rows)
+    and through NCCL all_to_all_single on the same inputs; True when every rank's
+    results agree bit for bit (one collective vote)."""
     from light_interaction_project_b200.ulysses import head_to_seq
     cfg, world, rank, hl = stack.cfg, stack.world, stack.rank, stack.hl
     B, s, _ = x.shape
-    D = cfg.head_dim
+    D, S = cfg.head_dim, s * world
+    q = stack.qkv_exchange(0, x)                                                   # peer path
+    got_q = q.permute(0, 2, 1, 3).reshape(S, hl * D).clone()
+    got_kv = stack.kv_buf[0][stack.kv_buf[0].shape[0] - S:].reshape(S, 2 * hl * D).clone()
     send = torch.matmul(x.reshape(B * s, cfg.hidden), stack.w_qkv_rank[0])          # [P, s, 3*hl*D]
-    row = 3 * hl * D * send.element_size()
-    got = stack.ex_qkv.push(send, s, row, s * row, row, rank * s * row, row)[: world * s * 3 * hl * D].clone()
     want = torch.empty_like(send)
     dist.all_to_all_single(want, send, group=group)
-    ok = torch.equal(got.view_as(want), want)
+    want = want.view(S, 3 * hl * D)
+    ok = torch.equal(got_q, want[:, : hl * D]) and torch.equal(got_kv, want[:, hl * D:])
     g = torch.Generator(device=x.device)
     g.manual_seed(99 + rank)
-    o_tok = torch.randn(B, world * s, hl, D, generator=g, device=x.device).to(torch.bfloat16)
+    o_tok = torch.randn(B, S, hl, D, generator=g, device=x.device).to(torch.bfloat16)
     row = hl * D * o_tok.element_size()
     got = stack.ex_out.push(o_tok, s, row, s * row, row, rank * row, cfg.heads * row // hl)
     got = got[: s * cfg.heads * D].view(B, s, cfg.heads, D).clone()
-    want = head_to_seq(o_tok.permute(0, 2, 1, 3), world, group)
-    ok = ok and torch.equal(got, want)
+    ok = ok and torch.equal(got, head_to_seq(o_tok.permute(0, 2, 1, 3), world, group))
     vote = torch.tensor([1 if ok else 0], device=x.device, dtype=torch.int32)
     dist.all_reduce(vote, op=dist.ReduceOp.MIN, group=group)
     torch.cuda.synchronize()

@@ -289,6 +289,13 @@ typedef struct li_a2a_desc {
   uint32_t* epoch_word;                 /* optional: the epoch kept on the device     */
   uint32_t epoch;                       /* 1, 2, ... per call, the same on all ranks  */
   int32_t world, rank;
+  /* Optional split rows (0: none). With split_bytes > 0 the first split_bytes
+   * of every row go to dst as above and the remaining row_bytes - split_bytes
+   * to dst2[p] + dst2_offset + r * dst2_row_stride (all 16-byte multiples). */
+  int64_t split_bytes;
+  void* dst2[LI_A2A_MAX_RANKS];         /* second destination of every rank          */
+  int64_t dst2_bytes;                   /* size of each second destination            */
+  int64_t dst2_offset, dst2_row_stride; /* bytes                                      */
 } li_a2a_desc;
 
 /* Chunk p of `src` (rows x row_bytes) -> rank p's receive buffer at dst_offset,

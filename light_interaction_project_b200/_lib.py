@@ -64,7 +64,9 @@ class A2ADesc(Structure):
                 ("rows", c_int64), ("row_bytes", c_int64), ("dst", c_void_p * A2A_MAX_RANKS),
                 ("dst_bytes", c_int64), ("dst_offset", c_int64), ("dst_row_stride", c_int64),
                 ("flags", c_void_p * A2A_MAX_RANKS), ("my_flags", c_void_p), ("counter", c_void_p),
-                ("err_word", c_void_p), ("epoch_word", c_void_p), ("epoch", c_uint32), ("world", c_int32), ("rank", c_int32)]
+                ("err_word", c_void_p), ("epoch_word", c_void_p), ("epoch", c_uint32), ("world", c_int32), ("rank", c_int32),
+                ("split_bytes", c_int64), ("dst2", c_void_p * A2A_MAX_RANKS), ("dst2_bytes", c_int64),
+                ("dst2_offset", c_int64), ("dst2_row_stride", c_int64)]
 
 
 class SelectParams(Structure):

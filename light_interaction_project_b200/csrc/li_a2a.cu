@@ -4,9 +4,11 @@
 // Every rank pushes: chunk p of its send buffer (rows of `row_bytes`) is
 // written with 16-byte stores straight into rank p's receive buffer, at a
 // per-source offset and row stride chosen by the caller (so the output side
-// lands directly in the [s, H, D] layout the O projection reads). No NCCL, no
-// copy engine, no multicast: plain st.global to peer addresses opened through
-// CUDA IPC.
+// lands directly in the [s, H, D] layout the O projection reads). A row may be
+// split: its first `split_bytes` go to the receive buffer and the rest to a
+// second buffer of rank p (the stack sends each token's q there and its k, v
+// straight into the rank's resident K/V buffer). No NCCL, no copy engine, no
+// multicast: plain st.global to peer addresses opened through CUDA IPC.
 //
 // Completion: each CTA fences its stores at system scope and takes a ticket;
 // the last CTA raises flag[rank] = epoch on every peer, then waits (bounded by
@@ -33,6 +35,9 @@ struct A2AArgs {
   int64_t src_chunk_stride, src_row_stride;  // bytes
   uint8_t* dst[LI_A2A_MAX_RANKS];            // receive-buffer base of every rank
   int64_t dst_offset, dst_row_stride;        // bytes, on every destination
+  uint8_t* dst2[LI_A2A_MAX_RANKS];           // second destination of every rank (split rows)
+  int64_t dst2_offset, dst2_row_stride;      // bytes
+  int64_t split_vecs;                        // 16-byte vectors of a row that go to dst (all: no split)
   int64_t rows, row_bytes;
   uint32_t* flags[LI_A2A_MAX_RANKS];         // flag array of every rank (slot = source rank)
   uint32_t* my_flags;
@@ -70,11 +75,13 @@ __global__ void __launch_bounds__(kA2AThreads) a2a_push_kernel(const A2AArgs a) 
   const int64_t n_cta = (gridDim.x - slot + W - 1) / W;  // CTAs serving this destination
   const uint8_t* src = a.src + p * a.src_chunk_stride;
   uint8_t* dst = a.dst[p] + a.dst_offset;
+  uint8_t* dst2 = a.split_vecs < v_per_row ? a.dst2[p] + a.dst2_offset : nullptr;
   for (int64_t i = (int64_t)(blockIdx.x / W) * kA2AThreads + threadIdx.x; i < v_per_chunk;
        i += n_cta * kA2AThreads) {
     const int64_t r = i / v_per_row, c = i % v_per_row;
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + r * a.src_row_stride) + c);
-    *(reinterpret_cast<uint4*>(dst + r * a.dst_row_stride) + c) = v;
+    if (c < a.split_vecs) *(reinterpret_cast<uint4*>(dst + r * a.dst_row_stride) + c) = v;
+    else *(reinterpret_cast<uint4*>(dst2 + r * a.dst2_row_stride) + (c - a.split_vecs)) = v;
   }
   __threadfence_system();
   __syncthreads();
@@ -156,8 +163,17 @@ extern "C" li_status li_a2a_push(const li_a2a_desc* d, void* stream) {
   if (!aligned16(d->src) || d->src_chunk_stride % 16 || d->src_row_stride % 16 || d->dst_offset % 16 ||
       d->dst_row_stride % 16)
     return fail(LI_ERR_ALIGNMENT, "exchange pointers, offsets and strides must be 16-byte multiples");
-  const int64_t dst_extent = d->dst_offset + (d->rows - 1) * d->dst_row_stride + d->row_bytes;
+  const bool split = d->split_bytes != 0;
+  if (split && (d->split_bytes < 16 || d->split_bytes >= d->row_bytes || d->split_bytes % 16 ||
+                d->dst2_offset % 16 || d->dst2_row_stride % 16 || d->dst2_offset < 0 || d->dst2_row_stride < 0))
+    return fail(LI_ERR_ALIGNMENT, "split_bytes must be a 16-byte multiple inside the row, and dst2 offsets 16-byte "
+                                  "multiples");
+  if (d->dst_offset < 0 || d->dst_row_stride < 0) return fail(LI_ERR_INVALID_ARG, "negative offset or stride");
+  const int64_t first = split ? d->split_bytes : d->row_bytes;
+  const int64_t dst_extent = d->dst_offset + (d->rows - 1) * d->dst_row_stride + first;
   if (dst_extent > d->dst_bytes) return fail(LI_ERR_OUT_OF_BOUNDS, "exchange writes past the receive buffer");
+  if (split && d->dst2_offset + (d->rows - 1) * d->dst2_row_stride + (d->row_bytes - first) > d->dst2_bytes)
+    return fail(LI_ERR_OUT_OF_BOUNDS, "exchange writes past the second destination");
   A2AArgs a;
   memset(&a, 0, sizeof(a));
   a.src = static_cast<const uint8_t*>(d->src);
@@ -167,8 +183,15 @@ extern "C" li_status li_a2a_push(const li_a2a_desc* d, void* stream) {
       return fail(LI_ERR_INVALID_ARG, "rank %d: receive buffer or flag array missing or unaligned", p);
     a.dst[p] = static_cast<uint8_t*>(d->dst[p]);
     a.flags[p] = d->flags[p];
+    if (split) {
+      if (!d->dst2[p] || !aligned16(d->dst2[p]))
+        return fail(LI_ERR_INVALID_ARG, "rank %d: second destination missing or unaligned", p);
+      a.dst2[p] = static_cast<uint8_t*>(d->dst2[p]);
+    }
   }
   a.dst_offset = d->dst_offset; a.dst_row_stride = d->dst_row_stride;
+  a.dst2_offset = d->dst2_offset; a.dst2_row_stride = d->dst2_row_stride;
+  a.split_vecs = first / 16;
   a.rows = d->rows; a.row_bytes = d->row_bytes;
   a.my_flags = d->my_flags; a.counter = d->counter; a.err = d->err_word; a.epoch_word = d->epoch_word;
   a.epoch = d->epoch; a.world = d->world; a.rank = d->rank;

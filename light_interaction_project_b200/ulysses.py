@@ -13,11 +13,14 @@ Here the exchange is one all-to-all per direction over the q/k/v stack (one
 exchange for all three), on the current stream: NCCL ``all_to_all_single``, or
 ``PeerExchange`` (``li_a2a_push``: 16-byte stores into the peers' CUDA-IPC
 receive buffers). The attention reads q straight from the all-to-all output
-through a strided view (no re-layout copy); K/V of the current chunk are written
-once into the tail of each layer's resident K/V buffer (the reference
-concatenates the cached context with the new chunk, ``hy patch:681-691``, which
-copies all of it). A whole step can be captured as one CUDA graph
-(:meth:`HeadShardedStack.capture`).
+through a strided view (no re-layout copy). With batch 1 each layer's resident
+K/V is token-major, so the current chunk's K/V rows are one contiguous block at
+its tail: the K/V projection writes them there directly at N = 1, and at N > 1
+the peer exchange stores each token's k and v straight into the owning rank's
+resident buffer (IPC-shared) while its q goes to the receive buffer. (The
+reference concatenates the cached context with the new chunk on every call,
+``hy patch:681-691``, which copies all of it.) A whole step can be captured as
+one CUDA graph (:meth:`HeadShardedStack.capture`).
 """
 
 from __future__ import annotations
@@ -134,8 +137,13 @@ class PeerExchange:
         return self.views[parity].view(dtype)
 
     def push(self, src: torch.Tensor, rows: int, row_bytes: int, src_chunk_stride: int, src_row_stride: int,
-             dst_offset: int, dst_row_stride: int) -> torch.Tensor:
-        """Exchange; returns this rank's receive buffer (flat, dtype of ``src``)."""
+             dst_offset: int, dst_row_stride: int, split=None) -> torch.Tensor:
+        """Exchange; returns this rank's receive buffer (flat, dtype of ``src``).
+
+        ``split`` = ``(split_bytes, dst2_ptrs, dst2_bytes, dst2_offset, dst2_row_stride)``:
+        the first ``split_bytes`` of every row go to the receive buffers as above,
+        the rest to ``dst2_ptrs[p]`` (one device pointer per rank, e.g. a
+        :class:`SharedBuffers` allocation) at ``dst2_offset + r * dst2_row_stride``."""
         L = self.L
         if not src.is_cuda or src.device != self.device:
             raise ValueError("send buffer must be on this rank's device")
@@ -159,12 +167,68 @@ class PeerExchange:
         # receive buffer, so a captured graph replays with fresh epochs.
         d.epoch_word = self.counter.data_ptr() + 4
         d.epoch, d.world, d.rank = self.epoch & 0xFFFFFFFF, self.world, self.rank
+        if split is not None:
+            d.split_bytes = split[0]
+            for q in range(self.world):
+                d.dst2[q] = split[1][q]
+            d.dst2_bytes, d.dst2_offset, d.dst2_row_stride = split[2], split[3], split[4]
         L.check(self.lib.li_a2a_push(L.ptr(d), L.stream_ptr(self.device)), "li_a2a_push")
         return self.recv_view(parity, src.dtype)
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (call after the last use
         has completed on every rank)."""
+        for p in self.mapped:
+            self.lib.li_ipc_close(p)
+        for p in self.own:
+            self.lib.li_ipc_free(p)
+        self.mapped, self.own = [], []
+
+
+class SharedBuffers:
+    """Device buffers that every rank's peer exchange may write into: each rank
+    allocates ``len(nbytes)`` zeroed buffers through CUDA IPC (``li_ipc_alloc``),
+    the handles are exchanged once over the process group, and every rank maps
+    its peers' buffers. ``tensor(i)`` is this rank's buffer ``i`` as a bf16
+    tensor; ``ptrs(i)`` lists buffer ``i`` of every rank (a peer's as mapped here)."""
+
+    def __init__(self, nbytes: List[int], rank: int, world: int, device, group=None):
+        import ctypes
+        self.L, self.lib = L, L.load()
+        self.rank, self.world, self.device = rank, world, torch.device(device)
+        self.nbytes = [int(n) for n in nbytes]
+        self.own, self.mapped, handles = [], [], []
+        for n in self.nbytes:
+            ptr, h = ctypes.c_void_p(), (ctypes.c_char * L.IPC_HANDLE_BYTES)()
+            L.check(self.lib.li_ipc_alloc(n, ctypes.byref(ptr), h), "li_ipc_alloc")
+            self.own.append(ptr.value)
+            handles.append(bytes(h))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, handles, group=group)
+        self._ptrs = [[0] * world for _ in self.nbytes]
+        for p in range(world):
+            for i, hb in enumerate(gathered[p]):
+                if p == rank:
+                    self._ptrs[i][p] = self.own[i]
+                    continue
+                ptr = ctypes.c_void_p()
+                L.check(self.lib.li_ipc_open(hb, ctypes.byref(ptr)), "li_ipc_open")
+                self.mapped.append(ptr.value)
+                self._ptrs[i][p] = ptr.value
+        self._views = [torch.as_tensor(_DeviceBuffer(self.own[i], n, self.device.index), device=self.device)
+                       .view(torch.bfloat16) for i, n in enumerate(self.nbytes)]
+        dist.barrier(group=group)
+
+    def tensor(self, i: int) -> torch.Tensor:
+        return self._views[i]
+
+    def ptrs(self, i: int) -> List[int]:
+        return self._ptrs[i]
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (after the last use has
+        completed on every rank)."""
+        self._views = []
         for p in self.mapped:
             self.lib.li_ipc_close(p)
         for p in self.own:
@@ -257,32 +321,55 @@ class HeadShardedStack:
                       for _ in range(cfg.layers)]
         self.w_o = [(torch.randn(hd, cfg.hidden, generator=gw, device=self.device) * std).to(dt)
                     for _ in range(cfg.layers)]
+        # Batch 1 keeps each layer's resident K/V token-major, [L, 2, H/P, D]: the current
+        # chunk's K and V rows are then one contiguous [S, 2*(H/P)*D] block at the tail,
+        # which the K/V projection (N = 1) or the peer exchange (N > 1) writes in place.
+        # Larger batches keep [B, 2, H/P, L, D] and write the tail with one gather launch.
+        self.token_major = cfg.batch == 1
+        # N = 1, batch 1: the Q and the K/V projections are separate GEMMs, the second
+        # writing straight into the resident buffer's tail.
+        self.w_q = self.w_kv = None
+        if world == 1 and self.token_major:
+            self.w_q = [w[:, :hd].contiguous() for w in self.w_qkv]
+            self.w_kv = [w[:, hd:].contiguous() for w in self.w_qkv]
         # N > 1, batch 1: the QKV projection writes the all-to-all send buffer directly.
         self.w_qkv_rank = ([rank_major_qkv_weight(w, world, cfg.heads, cfg.head_dim) for w in self.w_qkv]
                            if world > 1 and cfg.batch == 1 else None)
-        # N > 1, batch 1: both exchanges over NVLink peer memory; the output side lands
+        kv_tokens = cfg.kv_frames * cfg.frame_tokens
+        es = 2
+        # N > 1, batch 1: both exchanges over NVLink peer memory. The input side sends
+        # each token's q to the receive buffer and its k, v into the resident K/V
+        # buffer of the rank that owns those heads (IPC-shared); the output side lands
         # directly in the [s, H, D] rows the O projection reads.
-        self.ex_qkv = self.ex_out = None
+        self.ex_qkv = self.ex_out = self.kv_shared = None
         if world > 1 and cfg.batch == 1 and cfg.exchange == "peer":
             s = cfg.q_tokens // world
-            es = 2
-            self.ex_qkv = PeerExchange(world * s * 3 * self.hl * cfg.head_dim * es, rank, world, self.device, group)
+            self.ex_qkv = PeerExchange(world * s * self.hl * cfg.head_dim * es, rank, world, self.device, group)
             self.ex_out = PeerExchange(s * cfg.heads * cfg.head_dim * es, rank, world, self.device, group)
-        kv_tokens = cfg.kv_frames * cfg.frame_tokens
-        # K and V of a layer share one allocation [B, 2, H/P, L, D], so the current
-        # chunk's K and V are written by one gather launch (heads of K, then of V).
+            self.kv_shared = SharedBuffers([kv_tokens * 2 * self.hl * cfg.head_dim * es] * cfg.layers, rank, world,
+                                           self.device, group)
         self.kv_buf: List[torch.Tensor] = []
         self.k_buf: List[torch.Tensor] = []
         self.v_buf: List[torch.Tensor] = []
-        for _ in range(cfg.layers):
-            kv = torch.randn(cfg.batch, 2, self.hl, kv_tokens, cfg.head_dim, generator=g, device=self.device).to(dt)
-            self.kv_buf.append(kv)
-            self.k_buf.append(kv[:, 0])
-            self.v_buf.append(kv[:, 1])
+        for i in range(cfg.layers):
+            if self.token_major:
+                shape = (kv_tokens, 2, self.hl, cfg.head_dim)
+                kv = (self.kv_shared.tensor(i).view(shape) if self.kv_shared is not None
+                      else torch.empty(shape, device=self.device, dtype=dt))
+                kv.copy_(torch.randn(shape, generator=g, device=self.device))
+                self.kv_buf.append(kv)
+                self.k_buf.append(kv[:, 0].permute(1, 0, 2).unsqueeze(0))    # [1, H/P, L, D] views
+                self.v_buf.append(kv[:, 1].permute(1, 0, 2).unsqueeze(0))
+            else:
+                kv = torch.randn(cfg.batch, 2, self.hl, kv_tokens, cfg.head_dim, generator=g,
+                                 device=self.device).to(dt)
+                self.kv_buf.append(kv)
+                self.k_buf.append(kv[:, 0])
+                self.v_buf.append(kv[:, 1])
         nq, nk = cfg.blocks()
         self.q_block_offset = nk - nq
-        # Identity frame list: the current chunk's K/V go into the buffer tail
-        # through the library's 16-byte row-gather kernel.
+        # Batch > 1: identity frame list; the current chunk's K/V go into the buffer
+        # tail through the library's 16-byte row-gather kernel.
         self.chunk_frames = torch.arange(cfg.query_frames, dtype=torch.int32, device=self.device)
         # Pooled keys per layer: the memory frames are pooled once, each step
         # re-pools only the current chunk's block rows.
@@ -300,33 +387,48 @@ class HeadShardedStack:
         return torch.randn(self.cfg.batch, self.local_tokens(), self.cfg.hidden, generator=g,
                            device=self.device).to(torch.bfloat16)
 
-    def layer(self, i: int, x: torch.Tensor, attn_events=None) -> torch.Tensor:
+    def qkv_exchange(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        """Layer ``i``'s QKV projection and sequence->head exchange: writes the current
+        chunk's K/V rows into the layer's resident buffer (all of its S tokens, this
+        rank's heads) and returns q ``[B, H/P, S, D]`` (a strided view)."""
         cfg = self.cfg
         B, s, _ = x.shape
+        D, hl = cfg.head_dim, self.hl
+        S = s * self.world
+        tail = self.k_buf[i].shape[2] - S
+        if self.token_major and self.world == 1:
+            # Q projection, and the K/V projection written straight into the tail rows.
+            torch.matmul(x.reshape(s, cfg.hidden), self.w_kv[i], out=self.kv_buf[i][tail:].view(S, 2 * hl * D))
+            return (x.reshape(s, cfg.hidden) @ self.w_q[i]).view(1, S, hl, D).permute(0, 2, 1, 3)
         if self.ex_qkv is not None:
+            # One push per token row: q to the receive buffer, k and v straight into
+            # the tail of the owning rank's resident K/V buffer.
             send = torch.matmul(x.reshape(B * s, cfg.hidden), self.w_qkv_rank[i])   # [P, s, 3*hl*D]
-            row = 3 * self.hl * cfg.head_dim * send.element_size()
-            recv = self.ex_qkv.push(send, s, row, s * row, row, self.rank * s * row, row)
-            full = recv[: self.world * s * 3 * self.hl * cfg.head_dim].view(self.world * s, 3, 1, self.hl,
-                                                                                cfg.head_dim)
-        elif self.w_qkv_rank is not None:
+            row = 3 * hl * D * send.element_size()
+            qb = hl * D * send.element_size()
+            recv = self.ex_qkv.push(send, s, row, s * row, row, self.rank * s * qb, qb,
+                                    split=(qb, self.kv_shared.ptrs(i), self.kv_shared.nbytes[i],
+                                           (tail + self.rank * s) * 2 * qb, 2 * qb))
+            return recv[: S * hl * D].view(1, S, hl, D).permute(0, 2, 1, 3)
+        if self.w_qkv_rank is not None:
             full = qkv_to_head(x.reshape(B * s, cfg.hidden), self.w_qkv_rank[i], self.world, cfg.heads,
                                cfg.head_dim, self.group)                         # [S, 3, B, hl, D]
         else:
             qkv = (x.reshape(B * s, cfg.hidden) @ self.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
             full = seq_to_head(qkv.permute(2, 0, 1, 3, 4), self.world, self.group)   # [S, 3, B, hl, D]
-        S = full.shape[0]
-        q = full[:, 0].permute(1, 2, 0, 3)                                       # [B, hl, S, D] view
-        tail = self.k_buf[i].shape[2] - S
-        ft = cfg.frame_tokens
-        if B == 1:
-            # [S, 2, 1, hl, D] -> [1, 2*hl, S, D]: K heads then V heads, one launch.
-            src = full[:, 1:3].permute(2, 1, 3, 0, 4).view(1, 2 * self.hl, S, cfg.head_dim)
-            dst = self.kv_buf[i].view(1, 2 * self.hl, -1, cfg.head_dim)[:, :, tail:]
-            K.gather_frames(src, self.chunk_frames, ft, out=dst)
+        if self.token_major:
+            self.kv_buf[i][tail:].copy_(full[:, 1:3, 0])
         else:
+            ft = cfg.frame_tokens
             K.gather_frames(full[:, 1].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.k_buf[i][:, :, tail:])
             K.gather_frames(full[:, 2].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.v_buf[i][:, :, tail:])
+        return full[:, 0].permute(1, 2, 0, 3)                                    # [B, hl, S, D] view
+
+    def layer(self, i: int, x: torch.Tensor, attn_events=None) -> torch.Tensor:
+        cfg = self.cfg
+        B, s, _ = x.shape
+        S = s * self.world
+        q = self.qkv_exchange(i, x)
         # The attention writes its output token-major ([B, S, H/P, D]), the order the
         # return all-to-all / O projection reads, so no re-layout copy follows.
         o_tok = torch.empty(B, S, self.hl, cfg.head_dim, device=x.device, dtype=x.dtype)
@@ -351,10 +453,10 @@ class HeadShardedStack:
         """Releases the captured graph and the peer-exchange buffers (after the last
         step has completed on every rank)."""
         self._graph = None
-        for ex in (self.ex_qkv, self.ex_out):
+        for ex in (self.ex_qkv, self.ex_out, self.kv_shared):
             if ex is not None:
                 ex.close()
-        self.ex_qkv = self.ex_out = None
+        self.ex_qkv = self.ex_out = self.kv_shared = None
 
     def step(self, x: torch.Tensor, attn_events=None, check_errors: bool = False) -> torch.Tensor:
         """One step of every layer. ``check_errors``: synchronise afterwards and raise if

@@ -325,12 +325,15 @@ def test_mg_out_buffer_token_major(cuda_ok):
     assert torch.equal(buf.permute(0, 2, 1, 3), want)
 
 
-def test_stack_layer_matches_plain_restatement(cuda_ok):
-    """One head-sharded stack layer at N=1 (K/V written by the row-gather kernel,
-    attention output written token-major) equals the same layer written with
-    plain torch copies and the returned attention tensor."""
+@pytest.mark.parametrize("batch", [1, 2])
+def test_stack_layer_matches_plain_restatement(cuda_ok, batch):
+    """One head-sharded stack layer at N=1 equals the same layer written with plain
+    torch copies into separate K/V tensors and the returned attention tensor.
+    Batch 1: resident K/V token-major, the K/V projection writing the current
+    chunk's rows in place; batch 2: head-major K/V written by the row-gather kernel.
+    The attention output is written token-major in both."""
     from light_interaction_project_b200.ulysses import HeadShardedStack, StackConfig
-    cfg = StackConfig(layers=2, heads=4, hidden=512, memory_frames=4)
+    cfg = StackConfig(layers=2, heads=4, hidden=512, memory_frames=4, batch=batch)
     stack = HeadShardedStack(cfg, 0, 1, dev())
     x = stack.make_input()
     k_ref = [t.clone() for t in stack.k_buf]
@@ -338,9 +341,15 @@ def test_stack_layer_matches_plain_restatement(cuda_ok):
     y = stack.step(x)
     nq, nk = cfg.blocks()
     xr = x
+    hd = cfg.heads * cfg.head_dim
     for i in range(cfg.layers):
         B, s, _ = xr.shape
-        qkv = (xr.reshape(B * s, cfg.hidden) @ stack.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
+        x2 = xr.reshape(B * s, cfg.hidden)
+        if batch == 1:   # the stack's two projections (Q, then K/V)
+            qkv = torch.cat([x2 @ stack.w_q[i], x2 @ stack.w_kv[i]], dim=1).view(B, s, 3, cfg.heads, cfg.head_dim)
+        else:
+            qkv = (x2 @ stack.w_qkv[i]).view(B, s, 3, cfg.heads, cfg.head_dim)
+        assert qkv.shape[-1] * qkv.shape[-2] == hd
         q = qkv[:, :, 0].permute(0, 2, 1, 3)
         tail = k_ref[i].shape[2] - s
         k_ref[i][:, :, tail:].copy_(qkv[:, :, 1].permute(0, 2, 1, 3))

@@ -115,6 +115,38 @@ def test_exchange_single_rank_completes():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_exchange_split_rows_single_rank():
+    """Split rows: the first split_bytes of every row land in the receive buffer, the
+    rest in the second destination at its own offset and row stride (the stack
+    sends q to the receive buffer and k, v into the resident K/V buffer's tail)."""
+    from light_interaction_project_b200 import _lib as L
+    from light_interaction_project_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    K.device_errors(dev)
+    rows, row_bytes, split = 40, 96, 32
+    src = torch.randint(0, 255, (rows, row_bytes), dtype=torch.uint8, device=dev)
+    dst = torch.zeros(rows * split, dtype=torch.uint8, device=dev)
+    dst2 = torch.zeros(8 * 128 + rows * 128, dtype=torch.uint8, device=dev)   # 8 rows of head room, stride 128
+    flags = torch.zeros(4, dtype=torch.int32, device=dev)
+    counter = torch.zeros(4, dtype=torch.int32, device=dev)
+    d = _desc(L, K, src, [dst], [flags], counter, rows, row_bytes, 1, 0, dev)
+    d.dst_row_stride = split
+    d.split_bytes = split
+    d.dst2[0] = dst2.data_ptr()
+    d.dst2_bytes, d.dst2_offset, d.dst2_row_stride = dst2.numel(), 8 * 128, 128
+    L.check(L.load().li_a2a_push(L.ptr(d), L.stream_ptr(dev)), "li_a2a_push")
+    torch.cuda.synchronize()
+    assert torch.equal(dst.view(rows, split), src[:, :split])
+    body = dst2[8 * 128:].view(rows, 128)
+    assert torch.equal(body[:, : row_bytes - split], src[:, split:])
+    assert int(body[:, row_bytes - split:].abs().sum()) == 0 and int(dst2[: 8 * 128].abs().sum()) == 0
+    assert K.device_errors(dev) == 0
+    # A second destination too small for the rows is refused before any launch.
+    d.dst2_bytes = 8 * 128 + (rows - 1) * 128 + 32
+    assert L.load().li_a2a_push(L.ptr(d), L.stream_ptr(dev)) == L.LI_ERR_OUT_OF_BOUNDS
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
 def test_exchange_wait_runs_out_and_reports():
     """A peer that never joins: rank 0 of a world of 2 on one GPU, with nothing
     playing rank 1. The push still delivers both chunks (both buffers are local),
