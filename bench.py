@@ -50,6 +50,11 @@ def _peaks():
     return 1590.0, 1400.0, "fallback"
 
 
+def _hbm_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    return json.load(open(p)).get("hbm_gbs", 6650.0) if os.path.exists(p) else 6650.0
+
+
 def _profile_traffic(kernel_tag):
     """Per-launch DRAM bytes of the attention kernel from the committed ncu summary
     (a line ``traffic_bytes_per_launch: <int>`` in profiles/<kernel_tag>*.md)."""
@@ -219,7 +224,9 @@ def run_reference(args, cfg, rank, world):
 
 def workload_config(cfg, args, world):
     nq, nk = cfg.blocks()
-    return {"workload": "config5_head_sharded_stack" if args.workload == "stack" else "config3_mg_layer",
+    name = "config5_head_sharded_stack" if cfg.heads == 24 and cfg.layers == 30 else \
+        f"stack_{cfg.layers}layers_{cfg.heads}heads"
+    return {"workload": name if args.workload == "stack" else "config3_mg_layer",
             "layers": cfg.layers, "heads": cfg.heads, "head_dim": cfg.head_dim, "hidden": cfg.hidden,
             "latent_hw": list(cfg.latent_hw), "query_frames": cfg.query_frames,
             "memory_frames": cfg.memory_frames, "tile": list(cfg.tile), "keep_ratio": cfg.keep_ratio,
@@ -474,6 +481,16 @@ def run_gpu_layer(args, rank, world, local_rank):
         e.record()
         torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
+    # The retained-frame gather alone (K and V: 16 frames x 24 heads each), against
+    # the HBM copy peak: algorithmic bytes = read + write of the gathered rows.
+    s.record()
+    for _ in range(args.steps):
+        K.gather_frames(k_pool, ids, HW, out=k_buf[:, :, :16 * HW])
+        K.gather_frames(v_pool, ids, HW, out=v_buf[:, :, :16 * HW])
+    e.record()
+    torch.cuda.synchronize()
+    gather_ms = s.elapsed_time(e) / args.steps
+    gather_bytes = 2 * 2 * 16 * HW * H * 128 * 2      # (K, V) x (read, write)
     # Attention kernel alone.
     qp = K.pool_blocks(q, cfg.query_frames, LH, LW, cfg.tile)
     kp = K.pool_blocks(k_buf, cfg.kv_frames, LH, LW, cfg.tile)
@@ -499,6 +516,9 @@ def run_gpu_layer(args, rank, world, local_rank):
                           "value": fl * world / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_call": ms,
                           "attn_kernel_ms": attn_ms, "attn_kernel_tflops": fl / (attn_ms * 1e-3) / 1e12,
                           "frac_of_burst": fl / (attn_ms * 1e-3) / 1e12 / burst, "peak_kind": kind,
+                          "gather_ms": gather_ms, "gather_bytes": gather_bytes,
+                          "gather_gbs": gather_bytes / (gather_ms * 1e-3) / 1e9,
+                          "gather_frac_of_hbm": gather_bytes / (gather_ms * 1e-3) / 1e9 / _hbm_peak(),
                           "q_blocks": nq, "k_blocks": nk, "selected": cfg.budget(), "clocks": clk.summary()}),
               flush=True)
 
@@ -618,6 +638,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="stack", choices=["stack", "mg_layer", "configs"])
     ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--heads", type=int, default=24,
+                    help="attention heads of the stack (24 = config 5; 3 on one GPU is the per-rank shape at N = 8)")
     ap.add_argument("--warmup-ref", type=int, default=0)
     ap.add_argument("--cases", default="", help="--workload configs: regex selecting case names")
     ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
@@ -629,7 +651,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     from light_interaction_project_b200.ulysses import StackConfig
-    cfg = StackConfig(layers=args.layers, exchange=args.exchange)
+    cfg = StackConfig(layers=args.layers, heads=args.heads, exchange=args.exchange)
     if args.impl == "reference":
         run_reference(args, cfg, rank, world)
         return
