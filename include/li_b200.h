@@ -125,6 +125,22 @@ li_status li_tile_pool(const li_view4* src0, const li_view4* src1, const int32_t
 li_status li_pool_blocks(const li_view4* src, const int32_t* frame_ids, li_grid3d grid, li_view4* pool,
                          int64_t pool_block_offset, int32_t normalized, void* stream);
 
+/* Several li_pool_blocks jobs in one launch (1 to 4 jobs sharing the dtype and
+ * head dim; each keeps its own source, grid, pool and normalisation) — e.g. the
+ * q pool and the changed key-pool rows of one attention call, which the
+ * reference computes in its q-prep and kv-prep launches
+ * (ar_sparse_operation.py:166-202). Results are those of one li_pool_blocks
+ * call per job, bit for bit. */
+typedef struct li_pool_job {
+  const li_view4* src;
+  const int32_t* frame_ids;       /* optional, as in li_pool_blocks            */
+  li_grid3d grid;
+  li_view4* pool;
+  int64_t pool_block_offset;
+  int32_t normalized;
+} li_pool_job;
+li_status li_pool_blocks_multi(const li_pool_job* jobs, int32_t n_jobs, void* stream);
+
 /* Text K/V into the first blocks of the tiled K/V buffers, zero-padded to a
  * block multiple — replaces the F.pad + copy_ at ar_sparse_operation.py:337-344
  * (bi_sparse_operation_for_KV_cache.py:369-375; bi_sparse_operation.py:279-286).

@@ -55,6 +55,11 @@ class Grid3d(Structure):
     _fields_ = [("T", c_int32), ("LH", c_int32), ("LW", c_int32), ("tt", c_int32), ("th", c_int32), ("tw", c_int32)]
 
 
+class PoolJob(Structure):
+    _fields_ = [("src", POINTER(View4)), ("frame_ids", c_void_p), ("grid", Grid3d), ("pool", POINTER(View4)),
+                ("pool_block_offset", c_int64), ("normalized", c_int32)]
+
+
 A2A_MAX_RANKS = 8
 IPC_HANDLE_BYTES = 64
 
@@ -87,6 +92,7 @@ SIGNATURES = {
     "li_tile_pool": ([POINTER(View4), POINTER(View4), c_void_p, Grid3d, POINTER(View5), POINTER(View5), c_int64,
                       POINTER(View4), c_int64, c_void_p], c_int32),
     "li_pool_blocks": ([POINTER(View4), c_void_p, Grid3d, POINTER(View4), c_int64, c_int32, c_void_p], c_int32),
+    "li_pool_blocks_multi": ([POINTER(PoolJob), c_int32, c_void_p], c_int32),
     "li_text_blocks": ([POINTER(View4), POINTER(View4), c_int32, POINTER(View5), POINTER(View5), c_void_p], c_int32),
     "li_untile": ([POINTER(View5), Grid3d, POINTER(View4), c_void_p], c_int32),
     "li_gather_frames": ([POINTER(View4), c_void_p, c_int32, c_int32, POINTER(View4), c_void_p, c_void_p], c_int32),

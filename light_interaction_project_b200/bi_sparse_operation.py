@@ -39,7 +39,7 @@ def generate_prefill_indices(q_in, k_in, text_len, grid_thw, params, device, q_b
 
 
 def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params, q_block_offset=None, out=None,
-                         k_pool=None):
+                         k_pool=None, q_pool=None):
     """One Matrix-Game sparse-attention forward — ``bi_sparse_operation.py:236-348``.
 
     ``k``/``v`` hold ``text_len`` text tokens followed by the visual tokens. Dense
@@ -53,6 +53,10 @@ def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params,
     output projection reads it without a re-layout copy.
     ``k_pool`` (extension): a ``memory.KeyPoolCache`` refreshed by the caller for
     this ``k``'s visual part; the key pooling is then skipped.
+    ``q_pool`` (extension): q's block means ``[B, H, Nq_blk, D]`` computed by the
+    caller (normalised for the cosine metric), e.g. in the same
+    ``kernels.pool_blocks_multi`` launch as the key pool; the q pooling is then
+    skipped.
     Device-side errors (a bounded wait that gave up; a block id out of range)
     do not raise here: the kernels record them in the device error word, which
     ``kernels.raise_device_errors()`` reads (and synchronises) at a step boundary.
@@ -71,7 +75,7 @@ def run_sparse_attention(q, k, v, text_len, block_idx, latent_hw, sparse_params,
     out = sparse_forward(q, k[:, :, :text_len], v[:, :, :text_len], k[:, :, text_len:], v[:, :, text_len:],
                          latent_hw, sparse_params, L.SELECT_BIDIR, _DEFAULT_TILE,
                          ratio=sparse_params.get("topk_ratio", 0.25), q_block_offset=q_block_offset, profile=prof,
-                         out=out, k_pool=k_pool)
+                         out=out, k_pool=k_pool, q_pool=q_pool)
     if prof is not None:
         torch.cuda.synchronize()
         t = lambda a, b: prof[a].elapsed_time(prof[b])  # noqa: E731

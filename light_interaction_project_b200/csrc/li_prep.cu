@@ -7,6 +7,7 @@
 // chunk c of rows g, g+8, g+16, ... and, for the pooled stream, accumulates
 // those rows in fp64. The eight row-group partial sums are then combined in
 // order g = 0..7 — the summation order the CPU oracle restates.
+#include <algorithm>
 #include <cstring>
 
 #include "li_common.cuh"
@@ -71,14 +72,11 @@ constexpr int kMaxBS = 1024;
 // DT is the element type (LI_DTYPE_*), fixed at compile time so the per-element
 // widening carries no dtype branches.
 template <int DT>
-__global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
+__device__ __forceinline__ void tile_pool_block(const TileArgs& a, const int blk, const int bh, uint8_t* smem) {
   double* partial = reinterpret_cast<double*>(smem);                // [8][D]
   int32_t* rowtok = reinterpret_cast<int32_t*>(partial + 8 * a.D);  // token of each row, -1 = zero row
   float* prow = reinterpret_cast<float*>(rowtok + a.bs);            // [D] dtype-rounded means
   double* nrm = reinterpret_cast<double*>(smem);                    // [4] partial sums (reuses partial)
-  const int blk = blockIdx.x;
-  const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
   const int per_stream = 8 * a.CH;
   const int s = threadIdx.x / per_stream;
@@ -167,6 +165,33 @@ __global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
     for (int e = 0; e < epc; ++e)
       store_dt(pp, c * epc + e, round_dt(__fdiv_rn(prow[c * epc + e], den), DT), DT);
   }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(512) tile_pool_kernel(const TileArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  tile_pool_block<DT>(a, blockIdx.x, blockIdx.y, smem);
+}
+
+// Several pooling jobs in one launch (e.g. a layer's q and the changed rows of
+// its key pool): CTA i belongs to the job j with start[j] <= i < start[j+1] and
+// pools block (i - start[j]) % nblk_j of (b, h) = (i - start[j]) / nblk_j.
+constexpr int kMaxPoolJobs = 4;
+struct TileMulti {
+  TileArgs job[kMaxPoolJobs];
+  int64_t start[kMaxPoolJobs + 1];
+  int64_t nblk[kMaxPoolJobs];
+  int32_t n;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(512) tile_pool_multi_kernel(const __grid_constant__ TileMulti m) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int64_t i = blockIdx.x;
+  int j = 0;
+  while (j + 1 < m.n && i >= m.start[j + 1]) ++j;
+  const int64_t r = i - m.start[j];
+  tile_pool_block<DT>(m.job[j], (int)(r % m.nblk[j]), (int)(r / m.nblk[j]), smem);
 }
 
 struct UntileArgs {
@@ -289,9 +314,13 @@ using namespace li;
 
 namespace li {
 namespace {
-li_status tile_pool_impl(const li_view4* src0, const li_view4* src1, const int32_t* frame_ids, li_grid3d grid,
-                         li_view5* dst0, li_view5* dst1, int64_t dst_block_offset, li_view4* pool,
-                         int64_t pool_block_offset, int normalize, void* stream) {
+// Validates one tiling / pooling job and fills its kernel arguments; `nblk`,
+// `B`, `H` receive its grid. `*empty` is set when there is nothing to launch.
+li_status prepare_tile(const li_view4* src0, const li_view4* src1, const int32_t* frame_ids, li_grid3d grid,
+                       li_view5* dst0, li_view5* dst1, int64_t dst_block_offset, li_view4* pool,
+                       int64_t pool_block_offset, int normalize, TileArgs& a, int64_t& nblk, int64_t& B_out,
+                       int64_t& H_out, bool* empty) {
+  *empty = false;
   if (!src0) return fail(LI_ERR_INVALID_ARG, "src0 is required");
   if ((src1 == nullptr) != (dst1 == nullptr)) return fail(LI_ERR_INVALID_ARG, "dst1 must be given iff src1 is");
   if (li_status st = check_grid(grid)) return st;
@@ -304,12 +333,13 @@ li_status tile_pool_impl(const li_view4* src0, const li_view4* src1, const int32
   const int64_t src_frames = L / HW;
   if (!frame_ids && grid.T > src_frames)
     return fail(LI_ERR_SHAPE, "grid.T=%d exceeds the %lld frames of src0", grid.T, (long long)src_frames);
-  TileArgs a;
+  B_out = B;
+  H_out = H;
   memset(&a, 0, sizeof(a));
   a.bs = grid.tt * grid.th * grid.tw;
   a.T = grid.T; a.LH = grid.LH; a.LW = grid.LW; a.tt = grid.tt; a.th = grid.th; a.tw = grid.tw;
   a.nh = (int)ceil_div(grid.LH, grid.th); a.nw = (int)ceil_div(grid.LW, grid.tw);
-  const int64_t nblk = ceil_div(grid.T, grid.tt) * a.nh * a.nw;
+  nblk = ceil_div(grid.T, grid.tt) * a.nh * a.nw;
   a.H = (int)H; a.D = (int)D; a.dtype = dtype; a.CH = (int)(D * dtype_size(dtype) / 16);
   a.src_frames = (int)src_frames; a.frame_ids = frame_ids; a.flat = 0;
   a.nstreams = src1 ? 2 : 1;
@@ -337,14 +367,29 @@ li_status tile_pool_impl(const li_view4* src0, const li_view4* src1, const int32
     a.pool = static_cast<uint8_t*>(pool->data);
     a.p_b = pool->stride[0]; a.p_h = pool->stride[1]; a.p_n = pool->stride[2];
   }
-  if (!dst0 && !pool && !dst1) return LI_OK;
+  if (normalize && !pool) return fail(LI_ERR_INVALID_ARG, "normalised pooling needs a pool output");
+  if (!dst0 && !pool && !dst1) *empty = true;
   a.normalize = normalize;
   a.eps = dtype == LI_DTYPE_FP32 ? 1e-12f
         : dtype == LI_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(1e-12f))
                                  : __half2float(__float2half_rn(1e-12f));
-  if (normalize && !pool) return fail(LI_ERR_INVALID_ARG, "normalised pooling needs a pool output");
+  return LI_OK;
+}
+
+li_status tile_pool_impl(const li_view4* src0, const li_view4* src1, const int32_t* frame_ids, li_grid3d grid,
+                         li_view5* dst0, li_view5* dst1, int64_t dst_block_offset, li_view4* pool,
+                         int64_t pool_block_offset, int normalize, void* stream) {
+  TileArgs a;
+  int64_t nblk = 0, B = 0, H = 0;
+  bool empty = false;
+  if (li_status st = prepare_tile(src0, src1, frame_ids, grid, dst0, dst1, dst_block_offset, pool, pool_block_offset,
+                                  normalize, a, nblk, B, H, &empty))
+    return st;
+  if (empty) return LI_OK;
   return launch_tile(a, nblk, B, H, stream);
 }
+
+size_t tile_smem(const TileArgs& a) { return (size_t)8 * a.D * 8 + (size_t)a.bs * 4 + (size_t)a.D * 4; }
 }  // namespace
 }  // namespace li
 
@@ -360,6 +405,43 @@ extern "C" li_status li_pool_blocks(const li_view4* src, const int32_t* frame_id
                                     int64_t pool_block_offset, int32_t normalized, void* stream) {
   return tile_pool_impl(src, nullptr, frame_ids, grid, nullptr, nullptr, 0, pool, pool_block_offset,
                         normalized ? 1 : 0, stream);
+}
+
+extern "C" li_status li_pool_blocks_multi(const li_pool_job* jobs, int32_t n_jobs, void* stream) {
+  if (!jobs || n_jobs < 1 || n_jobs > kMaxPoolJobs)
+    return fail(LI_ERR_INVALID_ARG, "1 to %d pooling jobs are required (got %d)", kMaxPoolJobs, n_jobs);
+  TileMulti m;
+  memset(&m, 0, sizeof(m));
+  size_t smem = 0;
+  int64_t total = 0;
+  for (int j = 0; j < n_jobs; ++j) {
+    const li_pool_job& jb = jobs[j];
+    if (!jb.pool) return fail(LI_ERR_INVALID_ARG, "job %d: pool is required", j);
+    int64_t nblk = 0, B = 0, H = 0;
+    bool empty = false;
+    if (li_status st = prepare_tile(jb.src, nullptr, jb.frame_ids, jb.grid, nullptr, nullptr, 0, jb.pool,
+                                    jb.pool_block_offset, jb.normalized ? 1 : 0, m.job[m.n], nblk, B, H, &empty))
+      return st;
+    if (m.n > 0 && (m.job[m.n].dtype != m.job[0].dtype || m.job[m.n].CH != m.job[0].CH))
+      return fail(LI_ERR_INVALID_ARG, "job %d: every job must share the dtype and head dim of job 0", j);
+    if (nblk * B * H == 0) continue;
+    if (B * H > 65535) return fail(LI_ERR_SHAPE, "job %d: too many (batch, head) pairs", j);
+    m.start[m.n] = total;
+    m.nblk[m.n] = nblk;
+    total += nblk * B * H;
+    smem = std::max(smem, tile_smem(m.job[m.n]));
+    ++m.n;
+  }
+  if (m.n == 0) return LI_OK;
+  m.start[m.n] = total;
+  if (total > 2147483647) return fail(LI_ERR_SHAPE, "grid too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 block(8 * m.job[0].CH);
+  const unsigned grid = (unsigned)total;
+  if (m.job[0].dtype == LI_DTYPE_BF16) tile_pool_multi_kernel<LI_DTYPE_BF16><<<grid, block, smem, st>>>(m);
+  else if (m.job[0].dtype == LI_DTYPE_FP16) tile_pool_multi_kernel<LI_DTYPE_FP16><<<grid, block, smem, st>>>(m);
+  else tile_pool_multi_kernel<LI_DTYPE_FP32><<<grid, block, smem, st>>>(m);
+  return launched("tile_pool_multi_kernel launch");
 }
 
 extern "C" li_status li_text_blocks(const li_view4* src0, const li_view4* src1, int32_t bs,

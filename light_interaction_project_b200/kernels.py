@@ -92,6 +92,30 @@ def pool_blocks(x: torch.Tensor, T: int, LH: int, LW: int, tile, frame_ids=None,
     return pool
 
 
+def pool_blocks_multi(jobs):
+    """Several :func:`pool_blocks` jobs in one launch — ``li_pool_blocks_multi``. Each
+    job is a dict with ``src``, ``T``, ``LH``, ``LW``, ``tile``, ``out`` (the pool
+    tensor) and optionally ``block_offset``, ``normalized`` and ``frame_ids``; the
+    pools are written in place (bit-identical to one ``pool_blocks`` call each)."""
+    import ctypes
+    lib = L.load()
+    arr = (L.PoolJob * len(jobs))()
+    keep = []
+    for i, j in enumerate(jobs):
+        sv, pv = L.view4(j["src"], "src"), L.view4(j["out"], "pool")
+        keep += [sv, pv]
+        arr[i].src, arr[i].pool = ctypes.pointer(sv), ctypes.pointer(pv)
+        fid = j.get("frame_ids")
+        if fid is not None:
+            if fid.dtype != torch.int32 or not fid.is_cuda or not fid.is_contiguous() or fid.numel() < j["T"]:
+                raise ValueError("frame_ids must be a contiguous CUDA int32 tensor with one entry per logical frame")
+            arr[i].frame_ids = fid.data_ptr()
+        arr[i].grid = L.grid3d(j["T"], j["LH"], j["LW"], j["tile"])
+        arr[i].pool_block_offset = int(j.get("block_offset", 0))
+        arr[i].normalized = 1 if j.get("normalized", False) else 0
+    L.check(lib.li_pool_blocks_multi(arr, len(jobs), L.stream_ptr(jobs[0]["src"].device)), "li_pool_blocks_multi")
+
+
 def text_blocks(k_txt, v_txt, bs: int, k_all, v_all):
     lib = L.load()
     L.check(lib.li_text_blocks(L.ptr(L.view4(k_txt, "k_txt")), L.ptr(L.view4(v_txt, "v_txt")), int(bs),

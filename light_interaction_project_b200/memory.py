@@ -61,7 +61,11 @@ class KeyPoolCache:
         self.pool: Optional[torch.Tensor] = None
         self._shape = None
 
-    def refresh(self, k_vis: torch.Tensor, changed_from_frame: int = 0) -> "KeyPoolCache":
+    def pool_job(self, k_vis: torch.Tensor, changed_from_frame: int = 0):
+        """The pooling work :meth:`refresh` would launch, as a
+        ``kernels.pool_blocks_multi`` job (``None`` when nothing changed), so a
+        caller can pool these rows together with other pools in one launch. The
+        cache counts as refreshed once that job has run."""
         LH, LW = self.latent_hw
         HW = LH * LW
         if k_vis.shape[2] % HW:
@@ -77,10 +81,16 @@ class KeyPoolCache:
         tt = self.tile[0]
         f0 = (max(0, min(int(changed_from_frame), T)) // tt) * tt
         if f0 >= T:
-            return self
+            return None
         _, nh, nw = K.grid_blocks(T, LH, LW, self.tile)
-        K.pool_blocks(k_vis[:, :, f0 * HW:], T - f0, LH, LW, self.tile, normalized=self.metric == "cosine",
-                      out=self.pool, block_offset=(f0 // tt) * nh * nw)
+        return dict(src=k_vis[:, :, f0 * HW:], T=T - f0, LH=LH, LW=LW, tile=self.tile, out=self.pool,
+                    block_offset=(f0 // tt) * nh * nw, normalized=self.metric == "cosine")
+
+    def refresh(self, k_vis: torch.Tensor, changed_from_frame: int = 0) -> "KeyPoolCache":
+        job = self.pool_job(k_vis, changed_from_frame)
+        if job is not None:
+            K.pool_blocks(job["src"], job["T"], job["LH"], job["LW"], job["tile"], normalized=job["normalized"],
+                          out=job["out"], block_offset=job["block_offset"])
         return self
 
     def selection_pool(self, metric: str) -> torch.Tensor:

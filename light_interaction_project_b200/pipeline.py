@@ -40,7 +40,8 @@ def latent_grids(q_len: int, k_len: int, latent_hw, tile):
 def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode: int, default_tile,
                    default_metric: str = "cosine", ratio: Optional[float] = None, min_budget: int = 7,
                    q_block_offset: Optional[int] = None, score_bias: Optional[torch.Tensor] = None,
-                   profile: Optional[dict] = None, out: Optional[torch.Tensor] = None, k_pool=None):
+                   profile: Optional[dict] = None, out: Optional[torch.Tensor] = None, k_pool=None,
+                   q_pool: Optional[torch.Tensor] = None):
     LH, LW = latent_hw
     tile = tuple(int(x) for x in params.get("tile_size", default_tile))
     text_len = k_txt.shape[2] if k_txt is not None else 0
@@ -65,7 +66,13 @@ def sparse_forward(q, k_txt, v_txt, k_vis, v_vis, latent_hw, params: dict, mode:
     # keeps the normalisation out of the selection kernel's inner loop.
     cosine = metric == "cosine"
     mark("prep_start")
-    q_pool = K.pool_blocks(q, T_q, LH, LW, tile, normalized=cosine)
+    if q_pool is not None:
+        # Pooled by the caller (e.g. together with the key pool in one launch): the
+        # block means of q, normalised for the cosine metric.
+        if tuple(q_pool.shape) != (q.shape[0], q.shape[1], nq, q.shape[3]) or q_pool.dtype != q.dtype:
+            raise ValueError("q_pool does not match this call's query grid")
+    else:
+        q_pool = K.pool_blocks(q, T_q, LH, LW, tile, normalized=cosine)
     if k_pool is not None:
         # memory.KeyPoolCache: the key pool was refreshed by the caller (only the
         # block rows whose frames changed were re-pooled).

@@ -432,11 +432,22 @@ class HeadShardedStack:
         # The attention writes its output token-major ([B, S, H/P, D]), the order the
         # return all-to-all / O projection reads, so no re-layout copy follows.
         o_tok = torch.empty(B, S, self.hl, cfg.head_dim, device=x.device, dtype=x.dtype)
-        kp = self.key_pools[i].refresh(self.k_buf[i], changed_from_frame=cfg.memory_frames)
+        # One pooling launch for q and the current chunk's rows of the cached key
+        # pool (the memory frames' rows were pooled once and stay valid).
+        LH, LW = cfg.latent_hw
+        nq, _ = cfg.blocks()
+        q_pool = torch.empty(B, self.hl, nq, cfg.head_dim, device=x.device, dtype=x.dtype)
+        jobs = [dict(src=q, T=cfg.query_frames, LH=LH, LW=LW, tile=tuple(cfg.tile), out=q_pool,
+                     normalized=cfg.metric == "cosine")]
+        kjob = self.key_pools[i].pool_job(self.k_buf[i], changed_from_frame=cfg.memory_frames)
+        if kjob is not None:
+            jobs.append(kjob)
+        K.pool_blocks_multi(jobs)
         if attn_events is not None:
             attn_events[0].record()
         o = mg.run_sparse_attention(q, self.k_buf[i], self.v_buf[i], 0, i, cfg.latent_hw, self.params,
-                                    q_block_offset=self.q_block_offset, out=o_tok.permute(0, 2, 1, 3), k_pool=kp)
+                                    q_block_offset=self.q_block_offset, out=o_tok.permute(0, 2, 1, 3),
+                                    k_pool=self.key_pools[i], q_pool=q_pool)
         if attn_events is not None:
             attn_events[1].record()
         if self.ex_out is not None:

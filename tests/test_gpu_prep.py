@@ -144,3 +144,32 @@ def test_pool_blocks_normalized_equals_normalize_after_pool(cuda_ok, dtype, D):
     torch.cuda.synchronize()
     assert torch.equal(got[:, :, 5:], want)
     assert torch.isnan(got[:, :, :5]).all()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+def test_pool_blocks_multi_matches_separate_calls(cuda_ok, dtype):
+    """One li_pool_blocks_multi launch over three jobs (different grids and tiles, a
+    normalised pool, a fused frame gather, a block offset into a larger pool, a
+    token-major strided source) writes exactly what three li_pool_blocks calls do."""
+    D, LH, LW = 128 if dtype != "fp32" else 64, 10, 20
+    HW = LH * LW
+    _, q = rand((1, 3, 4 * HW, D), 871, dtype)
+    _, kv = rand((6 * HW, 2, 3, D), 872, dtype)                      # token-major [L, 2, H, D]
+    k = kv[:, 0].permute(1, 0, 2).unsqueeze(0)                         # [1, 3, L, D] strided view
+    _, pool_src = rand((1, 3, 8 * HW, D), 873, dtype)
+    ids = torch.tensor([6, 1, 3], dtype=torch.int32, device=dev())
+    t1, t2 = (4, 4, 8), (1, 8, 16)
+    nb = lambda T, t: int(np.prod(K.grid_blocks(T, LH, LW, t)))       # noqa: E731
+    want = [K.pool_blocks(q, 4, LH, LW, t1, normalized=True),
+            torch.zeros(1, 3, nb(6, t2) + 5, D, device=dev(), dtype=q.dtype),
+            K.pool_blocks(pool_src, 3, LH, LW, t1, frame_ids=ids)]
+    K.pool_blocks(k[:, :, 2 * HW:], 4, LH, LW, t2, out=want[1], block_offset=5 + nb(2, t2))
+    got = [torch.empty_like(want[0]), torch.zeros_like(want[1]), torch.empty_like(want[2])]
+    K.pool_blocks_multi([dict(src=q, T=4, LH=LH, LW=LW, tile=t1, out=got[0], normalized=True),
+                         dict(src=k[:, :, 2 * HW:], T=4, LH=LH, LW=LW, tile=t2, out=got[1],
+                              block_offset=5 + nb(2, t2)),
+                         dict(src=pool_src, T=3, LH=LH, LW=LW, tile=t1, out=got[2], frame_ids=ids)])
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    for g, w in zip(got, want):
+        assert torch.equal(g, w)
