@@ -43,6 +43,9 @@ typedef int32_t li_status;
 /* Bits OR-ed into the optional device error word (`err_word`) by kernels. */
 #define LI_DEVERR_BAD_INDEX   1u  /* a block index outside [0, n_kv_blocks)    */
 #define LI_DEVERR_TIMEOUT     2u  /* an mbarrier wait exceeded its bound       */
+#define LI_DEVERR_RANGE       4u  /* an fp32 attention operand beyond the fp16
+                                     range of the fp32 path (set by the Python
+                                     layer's operand conversion)               */
 
 /* ---- enums ------------------------------------------------------------- */
 #define LI_DTYPE_BF16 0

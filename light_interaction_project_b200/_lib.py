@@ -30,6 +30,7 @@ LI_ERR_TIMEOUT = 8
 
 LI_DEVERR_BAD_INDEX = 1
 LI_DEVERR_TIMEOUT = 2
+LI_DEVERR_RANGE = 4
 
 DTYPE_BF16, DTYPE_FP16, DTYPE_FP32 = 0, 1, 2
 METRIC_COSINE, METRIC_SCALED_DOT, METRIC_DOT = 0, 1, 2

@@ -628,7 +628,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const float a0 = l0 > 0.f ? ex2(m0 - mm) : 0.f, a1 = l1 > 0.f ? ex2(m1 - mm) : 0.f;
     const float lt = a0 * l0 + a1 * l1;
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
-    const bool store = ok && !*abort_flag;
+    // Warp-uniform: the TMEM loads below are warp-collective.
+    const bool store = __all_sync(0xFFFFFFFFu, ok && !*abort_flag);
     if (partial) {
       // Unnormalised partial of this split: O = a0 O_0 + a1 O_1 relative to mm.
       const int64_t unit = piece;
@@ -640,10 +641,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         for (int cc = 0; cc < kOCols / 32; ++cc) {
           const int col0 = w * kOCols + cc * 32;
           uint32_t x0[32], x1[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) { x0[e] = 0u; x1[e] = 0u; }
-          if (l0 > 0.f) tmem_ld32(o0 + col0, x0);
-          if (l1 > 0.f) tmem_ld32(o1 + col0, x1);
+          // tcgen05.ld is warp-collective: load both chains unconditionally and
+          // let each lane's l decide below (a NaN row sum must not split the warp).
+          tmem_ld32(o0 + col0, x0);
+          tmem_ld32(o1 + col0, x1);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
@@ -669,10 +670,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       for (int cc = 0; cc < kOCols / 32; ++cc) {
         const int col0 = w * kOCols + cc * 32;
         uint32_t x0[32], x1[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) { x0[e] = 0u; x1[e] = 0u; }
-        if (l0 > 0.f) tmem_ld32(o0 + col0, x0);
-        if (l1 > 0.f) tmem_ld32(o1 + col0, x1);
+        // tcgen05.ld is warp-collective: load both chains unconditionally and
+        // let each lane's l decide below (a NaN row sum must not split the warp).
+        tmem_ld32(o0 + col0, x0);
+        tmem_ld32(o1 + col0, x1);
         tmem_wait_ld();
         const float s0 = a0 * inv, s1 = a1 * inv;
         uint32_t pk[16];

@@ -45,6 +45,8 @@ def raise_device_errors(device=None):
         raise RuntimeError("li_b200: a device-side wait timed out")
     if v & L.LI_DEVERR_BAD_INDEX:
         raise ValueError("li_b200: an index (block id or frame id) was out of bounds")
+    if v & L.LI_DEVERR_RANGE:
+        raise ValueError("li_b200: an fp32 attention operand exceeded the fp16 range (|x| > 65504) of the fp32 path")
 
 
 def grid_blocks(T: int, LH: int, LW: int, tile: Sequence[int]) -> Tuple[int, int, int]:
@@ -239,8 +241,21 @@ def rank_blocks(rank_scores: torch.Tensor, score_dtype: torch.dtype, k: int, tex
 
 def _attn_operand(t: torch.Tensor) -> torch.Tensor:
     """Attention operands: bf16/fp16 with D contiguous and 16-byte strides
-    (copy only when the caller's layout cannot be described to TMA)."""
-    if t.dtype not in (torch.bfloat16, torch.float16):
+    (copy only when the caller's layout cannot be described to TMA).
+
+    fp32 operands become fp16: the reference's HY kernel feeds fp32 q/k/v to
+    ``tl.dot`` (tf32: 10 explicit mantissa bits, ``longcat_kernel.py`` HY
+    ``:126,141``), and fp16 keeps the same 10 bits, so the fp32 path computes at
+    the reference's precision. A finite fp32 value beyond fp16's range (|x| >
+    65504) would turn into an infinity: that sets ``LI_DEVERR_RANGE`` in the
+    device error word (no host synchronisation), which
+    :func:`raise_device_errors` reports."""
+    if t.dtype == torch.float32:
+        h = t.to(torch.float16)
+        flag = (torch.isinf(h) & torch.isfinite(t)).any().to(torch.int32) * L.LI_DEVERR_RANGE
+        error_word(t.device).bitwise_or_(flag)
+        t = h
+    elif t.dtype not in (torch.bfloat16, torch.float16):
         t = t.to(torch.bfloat16)
     ok = t.stride(-1) == 1 and all((s * 2) % 16 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 16 == 0
     return t if ok else t.contiguous()

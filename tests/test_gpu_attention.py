@@ -442,3 +442,50 @@ def test_many_tiles_random_lists(cuda_ok):
     fin = np.isfinite(ref_lse.reshape(B, H, -1))
     np.testing.assert_allclose(got_lse[fin], ref_lse.reshape(B, H, -1)[fin], atol=2e-3, rtol=1e-4)
     assert np.isneginf(got_lse[~fin]).all()
+
+
+@pytest.mark.parametrize("case", ["toy_config1", "mg_text"])
+def test_fp32_inputs_at_tf32_precision(cuda_ok, case):
+    """fp32 q/k/v (the CPU-runnable toy; and an MG call with text
+    tokens) against the fp32 oracle at a tf32-level tolerance: the fp32 path computes
+    with 10-bit-mantissa operands, the precision of the reference's tf32 ``tl.dot``."""
+    if case == "toy_config1":
+        B, H, D, LH, LW, Fq, Fk, tl = 1, 4, 64, 8, 8, 2, 6, 0
+        params = dict(tile_size=(2, 4, 8), topk_ratio=0.5, recent_protect=2, sim_metric="scaled_dot_product")
+    else:
+        B, H, D, LH, LW, Fq, Fk, tl = 1, 2, 128, 8, 16, 4, 4, 130
+        params = dict(tile_size=(4, 4, 8), topk_ratio=0.3, sim_metric="cosine")
+    HW = LH * LW
+    q, tq = rand((B, H, Fq * HW, D), 981, "fp32")
+    kt, tkt = rand((B, H, tl, D), 982, "fp32")
+    vt, tvt = rand((B, H, tl, D), 983, "fp32")
+    kv, tkv = rand((B, H, Fk * HW, D), 984, "fp32")
+    vv, tvv = rand((B, H, Fk * HW, D), 985, "fp32")
+    K.device_errors()
+    if case == "toy_config1":
+        out = ar.run_sparse_attention(tq, tkt, tvt, tkv, tvv, 3, (LH, LW), params)
+        ref, _ = O.run_sparse_attention_hy(q, kt, vt, kv, vv, (LH, LW), params, "fp32")
+    else:
+        k, v = np.concatenate([kt, kv], axis=2), np.concatenate([vt, vv], axis=2)
+        out = mg.run_sparse_attention(tq, to_gpu(k, "fp32"), to_gpu(v, "fp32"), tl, 3, (LH, LW), params)
+        ref, _ = O.run_sparse_attention_mg(q, k, v, tl, (LH, LW), params, "fp32")
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    assert out.dtype == torch.float32
+    assert_close_bf16(to_np(out), ref, max_abs=2e-3, mean_abs=2e-4, what=f"fp32 {case}")
+
+
+def test_fp32_operand_beyond_fp16_range_is_reported(cuda_ok):
+    """A finite fp32 operand that fp16 cannot hold is flagged in the device error word
+    and reported by raise_device_errors (the call itself does not synchronise)."""
+    B, H, D, bs = 1, 1, 64, 64
+    q, tq = rand((B, H, 2 * bs, D), 991, "fp32")
+    tk = tq.clone()
+    tk[0, 0, 5, 3] = 1.0e6
+    i = torch.tensor([[[[0, 1], [0, 1]]]], device=dev(), dtype=torch.int32)
+    c = torch.full((1, 1, 2), 2, device=dev(), dtype=torch.int32)
+    K.device_errors()
+    longcat_flash_attn(tq, tk, tq, i, c, logical_block_size=bs)
+    with pytest.raises(ValueError, match="fp16 range"):
+        K.raise_device_errors()
+    assert K.device_errors() == 0
