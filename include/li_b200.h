@@ -250,7 +250,8 @@ li_status li_rank_blocks(const li_view4* rank_scores, int32_t score_dtype, int32
  * workspace is allowed and simply disables the split. No reference
  * counterpart (the reference always launches one program per 128 query rows). */
 li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks,
-                                         int64_t max_blocks_per_row, int32_t head_dim, int64_t* bytes);
+                                         int64_t max_blocks_per_row, int32_t head_dim, int32_t block_size,
+                                         int64_t* bytes);
 
 /* Tiled form — replaces longcat_flash_attn / _attn_fwd_bsa_align
  * (hy-worldplay/.../longcat_kernel.py:27-233; matrix-game-3.0/.../longcat_kernel.py:28-190).
@@ -258,7 +259,10 @@ li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n
  * Query block i (rows i*bs .. i*bs+bs-1) attends to key blocks
  * indices[b,h,i,0:counts[b,h,i]]. o has q's shape; lse (optional fp32
  * [B,H,Q_len], log2 domain like the reference's M buffer) may be NULL.
- * D in {64, 128}; bs in {64, 128}; q/k/v/o bf16 or fp16 (all the same). */
+ * D in {64, 128}; bs in {32, 64, 128, 256} (the reference takes any power of two;
+ * a 256-token block runs as two 128-row halves, a block of 64 or 32 query rows
+ * fills the 128-row MMA tile with zero rows); q/k/v/o bf16 or fp16 (all the
+ * same). */
 li_status li_sparse_attn_tiled(const li_view4* q, const li_view4* k, const li_view4* v,
                                const li_index_view* idx, int32_t bs, float sm_scale,
                                li_view4* o, float* lse, uint32_t* err_word,

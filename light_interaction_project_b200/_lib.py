@@ -110,7 +110,8 @@ SIGNATURES = {
     "li_ipc_close": ([c_void_p], c_int32),
     "li_ipc_free": ([c_void_p], c_int32),
     "li_a2a_push": ([POINTER(A2ADesc), c_void_p], c_int32),
-    "li_sparse_attn_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, c_int32, POINTER(c_int64)], c_int32),
+    "li_sparse_attn_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, c_int32, c_int32, POINTER(c_int64)],
+                                       c_int32),
     "li_sparse_attn_tiled": ([POINTER(View4), POINTER(View4), POINTER(View4), POINTER(IndexView), c_int32, c_float,
                               POINTER(View4), c_void_p, c_void_p, c_void_p, c_int64, c_void_p], c_int32),
     "li_sparse_attn_raster": ([POINTER(View4), Grid3d, POINTER(View4), POINTER(View4), POINTER(View4),

@@ -96,6 +96,10 @@ struct __align__(64) Params {
   int32_t nsplit;
   float* part;
   int64_t part_units;
+  // Blocks of 256 tokens run as two 128-row sub-blocks (sub = 2, else 1). A
+  // sub-block's TMA box halves one tile dimension: c[*_split] of sub-block s is
+  // the block's origin + s * *_ext (for row layouts: split 1, ext = rows).
+  int32_t sub, q_split, q_ext, k_split, k_ext;
 };
 
 // ------------------------------- PTX helpers -------------------------------
@@ -317,6 +321,22 @@ __device__ __forceinline__ void block_coords(int raster, int blk, int bsz, int n
   c[4] = w;
 }
 
+// Row of the full (256-token) query block that row r of sub-block qs is; the
+// identity without sub-blocks. Raster sub-blocks halve dimension q_split.
+__device__ __forceinline__ int full_block_row(const Params& p, int r, int qs, int bsk) {
+  if (p.sub == 1) return r;
+  if (!p.q_raster) return qs * bsk + r;
+  int tw = p.q_tw, th = p.q_th, tt = p.q_tt;
+  if (p.q_split == 1) tw /= 2;
+  else if (p.q_split == 2) th /= 2;
+  else tt /= 2;
+  int ow = r % tw, rr = r / tw, oh = rr % th, ot = rr / th;
+  if (p.q_split == 1) ow += qs * tw;
+  else if (p.q_split == 2) oh += qs * th;
+  else ot += qs * tt;
+  return (ot * p.q_th + oh) * p.q_tw + ow;
+}
+
 // Named barrier over one chain's 4 softmax warps and the MMA warp. Every
 // participant executes it exactly once per block of the chain (work is
 // skipped, never the barrier, after an abort), so counts always match.
@@ -324,8 +344,9 @@ __device__ __forceinline__ void chain_sync(int chain) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + chain), "r"(160) : "memory");
 }
 
-// One TMA producer warp: loads tile j of every listed block into a ring of NST
-// stages (full barrier full0 + 8*stage, empty barrier empty0 + 8*stage). The
+// One TMA producer warp: loads tile j of every listed block (both sub-blocks of
+// a 256-token block, in order) into a ring of NST stages (full barrier
+// full0 + 8*stage, empty barrier empty0 + 8*stage). The
 // whole warp walks the list: lane l holds entry base + l of the current 32
 // entries, and the next 32 are already loading, so an index load never stands
 // between two copies; lane 0 waits for the stage and issues the copy. After an
@@ -338,42 +359,51 @@ __device__ __forceinline__ void produce(const Params& p, const int32_t* irow, in
                                         const CUtensorMap* txt_maps, volatile int* abort_flag, uint32_t bar_q) {
   int32_t cur = lane < S ? irow[(int64_t)lane * p.i_s] : 0;
   int32_t nxt = 32 + lane < S ? irow[(int64_t)(32 + lane) * p.i_s] : 0;
-  int issued = 0;
-  for (int j = 0; j < S; ++j) {
+  int issued = 0, jx = 0;  // jx: (sub-)blocks handed to the ring so far
+  bool go = true;
+  for (int j = 0; j < S && go; ++j) {
     if (j > 0 && (j & 31) == 0) {
       cur = nxt;
       nxt = j + 32 + lane < S ? irow[(int64_t)(j + 32 + lane) * p.i_s] : 0;
     }
-    int blk = __shfl_sync(0xFFFFFFFFu, cur, j & 31);
-    int ok = 1;
-    if (lane == 0) {
-      if (blk < 0 || blk >= p.n_kv) {
-        if (p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
-        blk = 0;
-      }
-      int c[5];
-      const CUtensorMap* m;
-      if (p.kv_raster && blk < p.ntxt) {
-        block_coords(0, blk, BS, 1, 1, 1, 1, 1, wc, c);
-        m = &txt_maps[mi];
-      } else {
-        block_coords(p.kv_raster, p.kv_raster ? blk - p.ntxt : blk, BS, p.k_nh, p.k_nw, p.k_tt,
-                     p.k_th, p.k_tw, wc, c);
-        m = &vis_maps[mi];
-      }
-      const int st = j % NST;
-      if (j >= NST && !mbar_wait(empty0 + 8 * st, ((j / NST) - 1) & 1, abort_flag, p.err)) {
-        ok = 0;
-      } else {
-        mbar_expect_tx(full0 + 8 * st, tile_bytes);
-        for (int hf = 0; hf < halves; ++hf) {
-          c[0] = 64 * hf;
-          tma_load_5d(ring + st * tile_bytes + hf * half_bytes, m, c, full0 + 8 * st);
+    const int blk0 = __shfl_sync(0xFFFFFFFFu, cur, j & 31);
+    for (int sb = 0; sb < p.sub; ++sb, ++jx) {
+      int ok = 1;
+      if (lane == 0) {
+        int blk = blk0;
+        if (blk < 0 || blk >= p.n_kv) {
+          if (p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
+          blk = 0;
         }
-        issued = j + 1;
+        int c[5];
+        const CUtensorMap* m;
+        if (p.kv_raster && blk < p.ntxt) {
+          block_coords(0, blk, BS * p.sub, 1, 1, 1, 1, 1, wc, c);
+          c[1] += sb * BS;
+          m = &txt_maps[mi];
+        } else {
+          block_coords(p.kv_raster, p.kv_raster ? blk - p.ntxt : blk, BS * p.sub, p.k_nh, p.k_nw, p.k_tt,
+                       p.k_th, p.k_tw, wc, c);
+          c[p.k_split] += sb * p.k_ext;
+          m = &vis_maps[mi];
+        }
+        const int st = jx % NST;
+        if (jx >= NST && !mbar_wait(empty0 + 8 * st, ((jx / NST) - 1) & 1, abort_flag, p.err)) {
+          ok = 0;
+        } else {
+          mbar_expect_tx(full0 + 8 * st, tile_bytes);
+          for (int hf = 0; hf < halves; ++hf) {
+            c[0] = 64 * hf;
+            tma_load_5d(ring + st * tile_bytes + hf * half_bytes, m, c, full0 + 8 * st);
+          }
+          issued = jx + 1;
+        }
+      }
+      if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) {
+        go = false;
+        break;
       }
     }
-    if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
   }
   if (lane == 0 && *abort_flag) {
     if (bar_q) mbar_wait(bar_q, 0, abort_flag, nullptr, false);
@@ -398,8 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     sp = (int)(piece % p.nsplit);
     ns = p.nsplit;
   }
-  const int qi = (int)(tile % p.nq);
-  const int bl = (int)(tile / p.nq) / p.H, h = (int)(tile / p.nq) % p.H;
+  const int64_t nqt = (int64_t)p.nq * p.sub;  // query tiles per (b, h)
+  const int qt = (int)(tile % nqt), qi = qt / p.sub, qs = qt % p.sub;
+  const int bl = (int)(tile / nqt) / p.H, h = (int)(tile / nqt) % p.H;
   const int b = p.b0 + bl;
   const int mi = p.per_batch ? bl : 0;
   const int wc = p.per_batch ? h : b * p.H + h;
@@ -422,10 +453,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const int S_all = S_raw < 0 ? 0 : (S_raw > p.smax ? p.smax : S_raw);
   if (S_all != S_raw && threadIdx.x == 0 && sp == 0 && p.err) atomicOr(p.err, (unsigned)LI_DEVERR_BAD_INDEX);
   const int j_lo = (int)(((int64_t)S_all * sp) / ns), j_hi = (int)(((int64_t)S_all * (sp + 1)) / ns);
-  const int S = j_hi - j_lo;  // this CTA's share of the list
+  const int S = j_hi - j_lo;  // this CTA's share of the list (entries)
+  const int SX = S * p.sub;   // (sub-)blocks it processes
   const int32_t* irow = p.idx + b * p.i_b + h * p.i_h + (int64_t)qi * p.i_q + (int64_t)j_lo * p.i_s;
   const bool partial = ns > 1;
-  const int n_chain[2] = {(S + 1) / 2, S / 2};  // blocks of chain 0 (even j) and chain 1 (odd j)
+  const int n_chain[2] = {(SX + 1) / 2, SX / 2};  // blocks of chain 0 (even j) and chain 1 (odd j)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -459,7 +491,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     if (S > 0) {
       if (warp == kWarpTMAK && lane == 0) {
         int c[5];
-        block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+        block_coords(p.q_raster, qi, BS * p.sub, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+        c[p.q_split] += qs * p.q_ext;
         mbar_expect_tx(bar_q, L::kTileBytes);
         for (int hf = 0; hf < L::kHalves; ++hf) {
           c[0] = 64 * hf;
@@ -505,12 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mma_commit(bar_ke(ks));
       mma_commit(bar_s(j & 1));
     };
-    if (lane == 0 && S > 0 && mbar_wait(bar_q, 0, abort_flag, p.err)) {
+    if (lane == 0 && SX > 0 && mbar_wait(bar_q, 0, abort_flag, p.err)) {
       tc_fence_after();
       issue_s(0);
-      if (S > 1) issue_s(1);
+      if (SX > 1) issue_s(1);
     }
-    for (int j = 0; j < S; ++j) {
+    for (int j = 0; j < SX; ++j) {
       const int c = j & 1;
       chain_sync(c);  // chain c's softmax has written P_j (or skipped after an abort)
       if (lane == 0 && !*abort_flag) {
@@ -524,12 +557,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int kk = 0; kk < BS / 16; ++kk)
             mma_ts(tO, tS + kk * 8, vd + (uint64_t)((kk * 2048) >> 4), idPV, (j >= 2 || kk > 0) ? 1u : 0u);
           mma_commit(bar_ve(vs));
-          if (j + 2 < S) issue_s(j + 2);
+          if (j + 2 < SX) issue_s(j + 2);
         }
       }
       __syncwarp();
     }
-    if (lane == 0 && S > 0) {
+    if (lane == 0 && SX > 0) {
       // Every MMA completes before O is read and TMEM is freed.
       for (int c = 0; c < 2; ++c)
         if (n_chain[c] > 0) mma_commit(bar_o(c));
@@ -699,7 +732,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     if (lane == 0) mbar_arrive(bar_st);
     if (store && !partial && threadIdx.x == 0 && mbar_wait(bar_st, 0, abort_flag, p.err) && !*abort_flag) {
       int c[5];
-      block_coords(p.q_raster, qi, BS, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+      block_coords(p.q_raster, qi, BS * p.sub, p.q_nh, p.q_nw, p.q_tt, p.q_th, p.q_tw, wc, c);
+      c[p.q_split] += qs * p.q_ext;
       for (int hf = 0; hf < L::kHalves; ++hf) {
         c[0] = 64 * hf;
         tma_store_5d(&p.o_map[mi], sb + L::kOffQ + hf * L::kQHalf, c);
@@ -707,7 +741,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tma_store_commit_and_drain();
     }
     if (store && !partial && w == 0 && p.lse && row < BS)
-      p.lse[(int64_t)(b * p.H + h) * p.lse_len + (int64_t)qi * BS + row] = lt > 0.f ? mm + __log2f(lt) : -INFINITY;
+      p.lse[(int64_t)(b * p.H + h) * p.lse_len + (int64_t)qi * BS * p.sub + full_block_row(p, row, qs, BS)] =
+          lt > 0.f ? mm + __log2f(lt) : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
@@ -738,14 +773,16 @@ struct CombineArgs {
   int32_t H, b0, nq, nsplit, D, bs, f16;
   int32_t q_raster, T, LH, LW, tt, th, tw, nh, nw;
   int64_t q_len;  // tiled form: valid query rows
+  int32_t sub, q_split, bsk;  // sub-blocks of a query block (rows bsk each), as in Params
 };
 
 __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const CombineArgs a) {
   __shared__ float wgt[kMaxPieces][kCombRows];
   __shared__ int64_t tok_s[kCombRows];
   const int64_t tile = a.n_whole + blockIdx.x;
-  const int qi = (int)(tile % a.nq);
-  const int b = a.b0 + (int)(tile / a.nq) / a.H, h = (int)(tile / a.nq) % a.H;
+  const int64_t nqt = (int64_t)a.nq * a.sub;
+  const int qt = (int)(tile % nqt), qi = qt / a.sub, qs = qt % a.sub;
+  const int b = a.b0 + (int)(tile / nqt) / a.H, h = (int)(tile / nqt) % a.H;
   const int bh = b * a.H + h;
   const int r0 = blockIdx.y * kCombRows;
   const int64_t unit0 = (int64_t)blockIdx.x * a.nsplit;
@@ -753,14 +790,31 @@ __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const Combin
   const float* pl = pm + a.part_units * 128;
   if (threadIdx.x < kCombRows) {
     const int row = r0 + threadIdx.x;
+    // Row of the full query block (sub-blocks halve dimension q_split).
+    int frow = row;
+    if (a.sub > 1) {
+      if (!a.q_raster) {
+        frow = qs * a.bsk + row;
+      } else {
+        int tw = a.tw, th = a.th, tt = a.tt;
+        if (a.q_split == 1) tw /= 2;
+        else if (a.q_split == 2) th /= 2;
+        else tt /= 2;
+        int ow = row % tw, rr = row / tw, oh = rr % th, ot = rr / th;
+        if (a.q_split == 1) ow += qs * tw;
+        else if (a.q_split == 2) oh += qs * th;
+        else ot += qs * tt;
+        frow = (ot * a.th + oh) * a.tw + ow;
+      }
+    }
     int64_t tok;
     if (a.q_raster) {
       const int cw = qi % a.nw, rem = qi / a.nw, ch = rem % a.nh, ct = rem / a.nh;
-      const int ow = row % a.tw, rr = row / a.tw, oh = rr % a.th, ot = rr / a.th;
+      const int ow = frow % a.tw, rr = frow / a.tw, oh = rr % a.th, ot = rr / a.th;
       const int t = ct * a.tt + ot, hh = ch * a.th + oh, w = cw * a.tw + ow;
       tok = (t < a.T && hh < a.LH && w < a.LW) ? ((int64_t)t * a.LH + hh) * a.LW + w : -1;
     } else {
-      tok = (int64_t)qi * a.bs + row;
+      tok = (int64_t)qi * a.bs + frow;
       if (tok >= a.q_len) tok = -1;
     }
     tok_s[threadIdx.x] = tok;
@@ -777,7 +831,7 @@ __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const Combin
       wgt[sp][threadIdx.x] = l > 0.f ? ex2(pm[(unit0 + sp) * 128 + row] - M) * inv : 0.f;
     }
     if (a.lse && tok >= 0)
-      a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + row] = L > 0.f ? M + __log2f(L) : -INFINITY;
+      a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + frow] = L > 0.f ? M + __log2f(L) : -INFINITY;
   }
   __syncthreads();
   const int cpr = a.D / 8;  // 8-column chunks per row
@@ -869,7 +923,7 @@ BHPlan plan_bh(const li_view4& v) {
 }
 
 // Raster operand: (d, w, h, t, bh); box = one (tt, th, tw) block.
-MapSpec raster_spec(const li_view4& v, const li_grid3d& g, const BHPlan& pl, int b, int es) {
+MapSpec raster_spec(const li_view4& v, const li_grid3d& g, const BHPlan& pl, int b, int es, int split = 0) {
   MapSpec s;
   const int64_t sl = v.stride[2] * es;
   s.base = static_cast<const uint8_t*>(v.data) + (pl.merged ? 0 : b * v.stride[0] * es);
@@ -878,7 +932,16 @@ MapSpec raster_spec(const li_view4& v, const li_grid3d& g, const BHPlan& pl, int
   s.strides[0] = (uint64_t)sl; s.strides[1] = (uint64_t)(sl * g.LW); s.strides[2] = (uint64_t)(sl * g.LW * g.LH);
   s.strides[3] = (uint64_t)(pl.w_stride * es);
   s.box[0] = 64; s.box[1] = (uint32_t)g.tw; s.box[2] = (uint32_t)g.th; s.box[3] = (uint32_t)g.tt; s.box[4] = 1;
+  if (split) s.box[split] /= 2;  // one 128-row sub-block of a 256-token block
   return s;
+}
+
+// The tile dimension a 256-token block is halved along (c / box index: 1 w,
+// 2 h, 3 t; the slowest even one), and the half extent.
+void sub_split(const li_grid3d& g, int32_t* split, int32_t* ext) {
+  if (g.tt % 2 == 0) { *split = 3; *ext = g.tt / 2; }
+  else if (g.th % 2 == 0) { *split = 2; *ext = g.th / 2; }
+  else { *split = 1; *ext = g.tw / 2; }
 }
 
 // Row operand: (d, rows, 1, 1, bh); box = bs consecutive rows.
@@ -943,11 +1006,11 @@ int64_t workspace_bytes(int64_t units, int64_t D) { return units * 128 * (D + 2)
 
 // Partial slots a call may need: one launch covers all B batches or, when the
 // operands' batch and head strides do not merge, at most kMaxMaps of them.
-int64_t call_units(int64_t B, int64_t H, int64_t nq, int64_t smax) {
+int64_t call_units(int64_t B, int64_t H, int64_t nq, int64_t smax, int sub) {
   int64_t u = 0;
   for (int64_t nb : {B, std::min<int64_t>(B, kMaxMaps), B % kMaxMaps}) {
-    const int64_t t = nb * H * nq;
-    u = std::max(u, plan_units(t, tail_plan(t, smax)));
+    const int64_t t = nb * H * nq * sub;
+    u = std::max(u, plan_units(t, tail_plan(t, smax * sub)));
   }
   return u;
 }
@@ -970,7 +1033,10 @@ li_status launch(int D, int BS, bool f16, const Params& prm, dim3 grid, cudaStre
   if (D == 128 && BS == 64) return f16 ? launch_t<128, 64, true>(prm, grid, s) : launch_t<128, 64, false>(prm, grid, s);
   if (D == 64 && BS == 128) return f16 ? launch_t<64, 128, true>(prm, grid, s) : launch_t<64, 128, false>(prm, grid, s);
   if (D == 64 && BS == 64) return f16 ? launch_t<64, 64, true>(prm, grid, s) : launch_t<64, 64, false>(prm, grid, s);
-  return fail(LI_ERR_UNSUPPORTED, "attention built for D in {64,128} and block size in {64,128} (got D=%d bs=%d)", D, BS);
+  if (D == 128 && BS == 32) return f16 ? launch_t<128, 32, true>(prm, grid, s) : launch_t<128, 32, false>(prm, grid, s);
+  if (D == 64 && BS == 32) return f16 ? launch_t<64, 32, true>(prm, grid, s) : launch_t<64, 32, false>(prm, grid, s);
+  return fail(LI_ERR_UNSUPPORTED, "attention built for D in {64,128} and block size in {32,64,128,256} (got D=%d bs=%d)",
+              D, BS);
 }
 
 li_status check_operand(const li_view4* v, const char* name, int dtype, int64_t B, int64_t H, int64_t D) {
@@ -996,7 +1062,10 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
   const int es = 2;
   const int64_t B = q->shape[0], H = q->shape[1], D = q->shape[3];
   if (D != 64 && D != 128) return fail(LI_ERR_UNSUPPORTED, "head dim %lld (built for 64 and 128)", (long long)D);
-  if (bs != 64 && bs != 128) return fail(LI_ERR_UNSUPPORTED, "block size %d (built for 64 and 128)", bs);
+  if (bs != 32 && bs != 64 && bs != 128 && bs != 256)
+    return fail(LI_ERR_UNSUPPORTED, "block size %d (built for 32, 64, 128, 256)", bs);
+  // 256-token blocks run as two 128-row sub-blocks.
+  const int sub = bs == 256 ? 2 : 1, bsk = bs / sub;
   for (const li_view4* t : {q, k, v, (const li_view4*)o})
     if (li_status st = check_operand(t, t == q ? "q" : t == k ? "k" : t == v ? "v" : "o", dtype, B, H, D)) return st;
   if (o->shape[2] != q->shape[2]) return fail(LI_ERR_SHAPE, "o must have q's shape");
@@ -1050,8 +1119,12 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
   prm.ntxt = ntxt; prm.n_kv = (int)n_kv; prm.nq = (int)nq;
   if (idx->shape[3] < 0 || idx->shape[3] > (1ll << 30)) return fail(LI_ERR_SHAPE, "bad index-row width");
   prm.smax = (int)idx->shape[3];
+  prm.sub = sub;
+  prm.q_split = 1; prm.q_ext = bsk; prm.k_split = 1; prm.k_ext = bsk;  // row layouts
+  if (sub > 1 && q_raster) sub_split(*gq, &prm.q_split, &prm.q_ext);
+  if (sub > 1 && kv_raster) sub_split(*gk, &prm.k_split, &prm.k_ext);
   if (nq == 0 || B * H == 0) return LI_OK;
-  if (B * H * nq > INT32_MAX) return fail(LI_ERR_SHAPE, "too many query tiles for one launch");
+  if (B * H * nq * sub > INT32_MAX) return fail(LI_ERR_SHAPE, "too many query tiles for one launch");
 
   // All operands share one (b, h) addressing plan; fall back to per-batch
   // maps when any operand's batch and head strides do not merge.
@@ -1072,29 +1145,30 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
         return x;
       };
       li_status st;
+      const int qsp = sub > 1 ? prm.q_split : 0, ksp = sub > 1 ? prm.k_split : 0;
       if (q_raster) {
-        st = encode(&prm.q_map[i], raster_spec(*q, *gq, pl(*q), bb, es), f16, "q");
-        if (!st) st = encode(&prm.o_map[i], raster_spec(*o, *gq, pl(*o), bb, es), f16, "o");
+        st = encode(&prm.q_map[i], raster_spec(*q, *gq, pl(*q), bb, es, qsp), f16, "q");
+        if (!st) st = encode(&prm.o_map[i], raster_spec(*o, *gq, pl(*o), bb, es, qsp), f16, "o");
       } else {
-        st = encode(&prm.q_map[i], rows_spec(*q, bs, pl(*q), bb, es), f16, "q");
-        if (!st) st = encode(&prm.o_map[i], rows_spec(*o, bs, pl(*o), bb, es), f16, "o");
+        st = encode(&prm.q_map[i], rows_spec(*q, bsk, pl(*q), bb, es), f16, "q");
+        if (!st) st = encode(&prm.o_map[i], rows_spec(*o, bsk, pl(*o), bb, es), f16, "o");
       }
       if (st) return st;
       if (kv_raster) {
-        st = encode(&prm.k_map[i], raster_spec(*k, *gk, pl(*k), bb, es), f16, "k");
-        if (!st) st = encode(&prm.v_map[i], raster_spec(*v, *gk, pl(*v), bb, es), f16, "v");
-        if (!st && ntxt) st = encode(&prm.kt_map[i], rows_spec(*kt, bs, pl(*kt), bb, es), f16, "k_txt");
-        if (!st && ntxt) st = encode(&prm.vt_map[i], rows_spec(*vt, bs, pl(*vt), bb, es), f16, "v_txt");
+        st = encode(&prm.k_map[i], raster_spec(*k, *gk, pl(*k), bb, es, ksp), f16, "k");
+        if (!st) st = encode(&prm.v_map[i], raster_spec(*v, *gk, pl(*v), bb, es, ksp), f16, "v");
+        if (!st && ntxt) st = encode(&prm.kt_map[i], rows_spec(*kt, bsk, pl(*kt), bb, es), f16, "k_txt");
+        if (!st && ntxt) st = encode(&prm.vt_map[i], rows_spec(*vt, bsk, pl(*vt), bb, es), f16, "v_txt");
       } else {
-        st = encode(&prm.k_map[i], rows_spec(*k, bs, pl(*k), bb, es), f16, "k");
-        if (!st) st = encode(&prm.v_map[i], rows_spec(*v, bs, pl(*v), bb, es), f16, "v");
+        st = encode(&prm.k_map[i], rows_spec(*k, bsk, pl(*k), bb, es), f16, "k");
+        if (!st) st = encode(&prm.v_map[i], rows_spec(*v, bsk, pl(*v), bb, es), f16, "v");
       }
       if (st) return st;
     }
     // Tail split of this launch's tiles, when the workspace holds its partials
     // (launches run in stream order, so every launch reuses the workspace).
-    const int64_t tiles = nb * H * nq;
-    TailPlan tp = tail_plan(tiles, prm.smax);
+    const int64_t tiles = nb * H * nq * sub;
+    TailPlan tp = tail_plan(tiles, (int64_t)prm.smax * sub);
     const int64_t units = plan_units(tiles, tp);
     if (tp.pieces > 1 && !(workspace && workspace_bytes_avail >= workspace_bytes(units, D) && aligned16(workspace)))
       tp = TailPlan{tiles, 1};
@@ -1103,7 +1177,7 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
     prm.part = tp.pieces > 1 ? static_cast<float*>(workspace) : nullptr;
     prm.part_units = tp.pieces > 1 ? units : 0;
     dim3 grid((unsigned)(tp.n_whole + prm.part_units));
-    if (li_status st = launch((int)D, bs, f16, prm, grid, static_cast<cudaStream_t>(stream))) return st;
+    if (li_status st = launch((int)D, bsk, f16, prm, grid, static_cast<cudaStream_t>(stream))) return st;
     if (tp.pieces > 1) {
       CombineArgs ca;
       memset(&ca, 0, sizeof(ca));
@@ -1117,7 +1191,8 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
         ca.nh = prm.q_nh; ca.nw = prm.q_nw;
       }
       ca.q_len = q->shape[2];
-      attn_combine_kernel<<<dim3((unsigned)(tiles - tp.n_whole), (unsigned)(bs / kCombRows)), kCombThreads, 0,
+      ca.sub = sub; ca.q_split = prm.q_split; ca.bsk = bsk;
+      attn_combine_kernel<<<dim3((unsigned)(tiles - tp.n_whole), (unsigned)(bsk / kCombRows)), kCombThreads, 0,
                             static_cast<cudaStream_t>(stream)>>>(ca);
       if (li_status st = launched("attention combine launch")) return st;
     }
@@ -1131,9 +1206,12 @@ li_status run(const li_view4* q, bool q_raster, const li_grid3d* gq, const li_vi
 using namespace li;
 
 extern "C" li_status li_sparse_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t n_q_blocks,
-                                                    int64_t max_blocks_per_row, int32_t head_dim, int64_t* bytes) {
+                                                    int64_t max_blocks_per_row, int32_t head_dim, int32_t block_size,
+                                                    int64_t* bytes) {
   if (!bytes) return fail(LI_ERR_INVALID_ARG, "bytes is required");
-  *bytes = attn::workspace_bytes(attn::call_units(batch, heads, n_q_blocks, max_blocks_per_row), head_dim);
+  if (batch < 0 || heads < 0 || n_q_blocks < 0 || max_blocks_per_row < 0) return fail(LI_ERR_SHAPE, "negative shape");
+  *bytes = attn::workspace_bytes(attn::call_units(batch, heads, n_q_blocks, max_blocks_per_row, block_size == 256 ? 2 : 1),
+                                 head_dim);
   return LI_OK;
 }
 

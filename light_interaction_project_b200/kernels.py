@@ -261,14 +261,14 @@ def _attn_operand(t: torch.Tensor) -> torch.Tensor:
     return t if ok else t.contiguous()
 
 
-def attn_workspace(B: int, H: int, nq: int, smax: int, D: int, device):
+def attn_workspace(B: int, H: int, nq: int, smax: int, D: int, device, bs: int = 128):
     """Split-KV scratch for one attention call (``li_sparse_attn_workspace_bytes``),
     from torch's caching allocator; ``(tensor or None, bytes)``."""
     import ctypes
     lib = L.load()
     nbytes = ctypes.c_int64()
-    L.check(lib.li_sparse_attn_workspace_bytes(int(B), int(H), int(nq), int(smax), int(D), ctypes.byref(nbytes)),
-            "li_sparse_attn_workspace_bytes")
+    L.check(lib.li_sparse_attn_workspace_bytes(int(B), int(H), int(nq), int(smax), int(D), int(bs),
+                                               ctypes.byref(nbytes)), "li_sparse_attn_workspace_bytes")
     if nbytes.value == 0:
         return None, 0
     return torch.empty(nbytes.value, dtype=torch.uint8, device=device), nbytes.value
@@ -290,7 +290,7 @@ def sparse_attn_tiled(q, k, v, indices, counts, bs: int, sm_scale: Optional[floa
     o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     nq = (q.shape[2] + bs - 1) // bs
     lse = torch.empty((q.shape[0], q.shape[1], nq * bs), device=q.device, dtype=torch.float32) if return_lse else None
-    ws, wsb = attn_workspace(q.shape[0], q.shape[1], nq, indices.shape[3], D, q.device)
+    ws, wsb = attn_workspace(q.shape[0], q.shape[1], nq, indices.shape[3], D, q.device, bs)
     L.check(lib.li_sparse_attn_tiled(L.ptr(L.view4(q, "q")), L.ptr(L.view4(k, "k")), L.ptr(L.view4(v, "v")),
                                      L.ptr(L.index_view(indices, counts)), int(bs), float(sm_scale),
                                      L.ptr(L.view4(o, "o")), lse.data_ptr() if lse is not None else None,
@@ -325,7 +325,7 @@ def sparse_attn_raster(q, grid_q: L.Grid3d, k_txt, v_txt, k_vis, v_vis, grid_k: 
     nt, nh, nw = grid_blocks(grid_q.T, grid_q.LH, grid_q.LW, (grid_q.tt, grid_q.th, grid_q.tw))
     lse = (torch.empty((q.shape[0], q.shape[1], nt * nh * nw * bs), device=q.device, dtype=torch.float32)
            if return_lse else None)
-    ws, wsb = attn_workspace(q.shape[0], q.shape[1], nt * nh * nw, indices.shape[3], D, q.device)
+    ws, wsb = attn_workspace(q.shape[0], q.shape[1], nt * nh * nw, indices.shape[3], D, q.device, bs)
     L.check(lib.li_sparse_attn_raster(
         L.ptr(L.view4(q, "q")), grid_q, L.ptr(L.view4(k_txt, "k_txt")) if have_txt else None,
         L.ptr(L.view4(v_txt, "v_txt")) if have_txt else None, L.ptr(L.view4(k_vis, "k_vis")),

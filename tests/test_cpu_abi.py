@@ -110,15 +110,15 @@ def test_split_plan_workspace(lib):
     each) are cut into list pieces; the workspace holds exactly their partials."""
     nbytes = ctypes.c_int64()
     unit = 128 * 130 * 4   # one fp32 partial tile of D=128: O, row max, row sum
-    assert lib.li_sparse_attn_workspace_bytes(1, 24, 56, 238, 128, ctypes.byref(nbytes)) == 0
+    assert lib.li_sparse_attn_workspace_bytes(1, 24, 56, 238, 128, 128, ctypes.byref(nbytes)) == 0
     assert nbytes.value == 12 * 12 * unit        # 1344 tiles = 9 waves + 12: each of the 12 in 12 pieces
-    assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 238, 128, ctypes.byref(nbytes)) == 0
+    assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 238, 128, 128, ctypes.byref(nbytes)) == 0
     assert nbytes.value == 20 * 7 * unit         # 168 tiles = 1 wave + 20: 7 pieces each
-    assert lib.li_sparse_attn_workspace_bytes(1, 16, 64, 256, 128, ctypes.byref(nbytes)) == 0
+    assert lib.li_sparse_attn_workspace_bytes(1, 16, 64, 256, 128, 128, ctypes.byref(nbytes)) == 0
     assert nbytes.value == 0                     # 1024 tiles = 6 waves + 136: last wave nearly full
-    assert lib.li_sparse_attn_workspace_bytes(1, 148, 1, 100, 128, ctypes.byref(nbytes)) == 0
+    assert lib.li_sparse_attn_workspace_bytes(1, 148, 1, 100, 128, 128, ctypes.byref(nbytes)) == 0
     assert nbytes.value == 0                     # whole waves
-    assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 8, 128, ctypes.byref(nbytes)) == 0
+    assert lib.li_sparse_attn_workspace_bytes(1, 3, 56, 8, 128, 128, ctypes.byref(nbytes)) == 0
     assert nbytes.value == 0                     # too few blocks per row to split
 
 

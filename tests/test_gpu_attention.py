@@ -36,7 +36,8 @@ def _random_lists(rng, B, H, nq, nkb, S, vary=True):
     return idx, cnt
 
 
-@pytest.mark.parametrize("D,bs", [(128, 128), (128, 64), (64, 128), (64, 64)])
+@pytest.mark.parametrize("D,bs", [(128, 128), (128, 64), (64, 128), (64, 64), (128, 256), (64, 256), (128, 32),
+                                  (64, 32)])
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 def test_tiled_attention_vs_oracle(cuda_ok, D, bs, dtype):
     B, H, nq, nkb, S = 1, 3, 5, 9, 4
@@ -238,7 +239,7 @@ def test_reference_fixtures_end_to_end(cuda_ok, name):
             assert_close_bf16(got[b, h, rows], ref_rows, what=f"{name} b{b} h{h}")
 
 
-@pytest.mark.parametrize("D,bs", [(128, 128), (64, 64)])
+@pytest.mark.parametrize("D,bs", [(128, 128), (64, 64), (128, 256), (64, 32)])
 def test_split_kv_partials_merge(cuda_ok, D, bs):
     """Few query blocks -> the list of each is split over CTAs writing fp32
     partials (some splits empty) that the combine kernel merges."""
@@ -246,7 +247,7 @@ def test_split_kv_partials_merge(cuda_ok, D, bs):
     import ctypes
     B, H, nq, nkb, S = 1, 2, 5, 60, 40
     nb = ctypes.c_int64()
-    LL.load().li_sparse_attn_workspace_bytes(B, H, nq, S, D, ctypes.byref(nb))
+    LL.load().li_sparse_attn_workspace_bytes(B, H, nq, S, D, bs, ctypes.byref(nb))
     assert nb.value > 0, "this shape must take the split path"
     q, tq = rand((B, H, nq * bs, D), 901, "bf16")
     k, tk = rand((B, H, nkb * bs, D), 902, "bf16")
@@ -489,3 +490,35 @@ def test_fp32_operand_beyond_fp16_range_is_reported(cuda_ok):
     with pytest.raises(ValueError, match="fp16 range"):
         K.raise_device_errors()
     assert K.device_errors() == 0
+
+
+@pytest.mark.parametrize("tile", [(4, 8, 8), (1, 16, 16), (1, 1, 256), (2, 4, 4), (1, 4, 8)],
+                         ids=["bs256_t", "bs256_h", "bs256_w", "bs32_t", "bs32"])
+def test_raster_block_sizes_256_and_32(cuda_ok, tile):
+    """Block sizes beyond 64/128 through the HY decode and MG operators (raster q,
+    K/V and text read in place, output untiled by the store): 256-token blocks run
+    as two 128-row halves split along t, h or w; 32-token blocks fill the 128-row
+    MMA tile with zero rows. Against the oracle, selection bit-exact."""
+    bs = tile[0] * tile[1] * tile[2]
+    LH, LW = (16, 32) if tile != (1, 1, 256) else (4, 256)
+    H, D = 2, 128
+    HW = LH * LW
+    for kind in ("hy", "mg"):
+        Fq, Fk, tl = (4, 8, 40) if kind == "hy" else (4, 4, 300)
+        q, tq = rand((1, H, Fq * HW, D), 1101, "bf16")
+        kt, tkt = rand((1, H, tl, D), 1102, "bf16")
+        vt, tvt = rand((1, H, tl, D), 1103, "bf16")
+        kv, tkv = rand((1, H, Fk * HW, D), 1104, "bf16")
+        vv, tvv = rand((1, H, Fk * HW, D), 1105, "bf16")
+        if kind == "hy":
+            params = dict(tile_size=tile, topk_ratio=0.3, recent_protect=2, sim_metric="scaled_dot_product")
+            out = ar.run_sparse_attention(tq, tkt, tvt, tkv, tvv, 3, (LH, LW), params)
+            ref, aux = O.run_sparse_attention_hy(q, kt, vt, kv, vv, (LH, LW), params, "bf16")
+        else:
+            params = dict(tile_size=tile, topk_ratio=0.4, sim_metric="cosine")
+            k, v = np.concatenate([kt, kv], axis=2), np.concatenate([vt, vv], axis=2)
+            out = mg.run_sparse_attention(tq, to_gpu(k, "bf16"), to_gpu(v, "bf16"), tl, 3, (LH, LW), params)
+            ref, aux = O.run_sparse_attention_mg(q, k, v, tl, (LH, LW), params, "bf16")
+        torch.cuda.synchronize()
+        assert K.device_errors() == 0
+        assert_close_bf16(to_np(out), ref, what=f"{kind} tile {tile} (bs {bs})")
