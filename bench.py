@@ -4,8 +4,9 @@ Default workload (the one the metric is quoted on at
 1/2/4/8 GPUs): a head-sharded full-stack step — 30 attention layers of the
 Matrix-Game shape (24 heads, head_dim 128, 30x52 latent, 4-frame query chunk,
 64-frame memory, 3D blocks (4,4,8), keep 25%, cosine selection), QKV/O
-projections of hidden 3072 (random-init bf16), Ulysses all-to-all over NCCL
-before and after each attention when N > 1. ``--workload mg_layer`` runs
+projections of hidden 3072 (random-init bf16), Ulysses all-to-all before and
+after each attention when N > 1 (NVLink peer pushes by default, checked bit for
+bit against NCCL before timing; ``--exchange nccl`` for NCCL itself). ``--workload mg_layer`` runs
 BASELINE config 3 instead (single MG-shaped layer with the pruned-memory gather).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload W]
@@ -21,6 +22,7 @@ block-mask logic + dense masked torch attention) on the host cores.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import math
 import os
@@ -297,7 +299,9 @@ def run_gpu(args, cfg, rank, world, local_rank):
     stack = HeadShardedStack(cfg, rank, world, dev, group=group)
     x0 = stack.make_input()
     # N > 1 with the peer exchange: check it bit for bit against NCCL on this box
-    # before anything is timed; on a mismatch every rank falls back to NCCL.
+    # before anything is timed; on a mismatch every rank falls back to NCCL. The
+    # stack is rebuilt for that, since its resident K/V buffers are the IPC-shared
+    # ones the closed exchange owned.
     exch = None
     if world > 1:
         exch = {"transport": cfg.exchange, "check": None}
@@ -305,7 +309,12 @@ def run_gpu(args, cfg, rank, world, local_rank):
             ok = exchange_check(stack, x0, group)
             exch["check"] = ok
             if not ok:
+                torch.cuda.synchronize()
+                dist.barrier()
                 stack.close()
+                del x0
+                stack = HeadShardedStack(dataclasses.replace(cfg, exchange="nccl"), rank, world, dev, group=group)
+                x0 = stack.make_input()
                 exch["transport"] = "nccl (peer exchange failed its check)"
 
     def barrier():

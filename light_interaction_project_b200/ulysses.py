@@ -462,8 +462,12 @@ class HeadShardedStack:
 
     def close(self):
         """Releases the captured graph and the peer-exchange buffers (after the last
-        step has completed on every rank)."""
+        step has completed on every rank). With the peer exchange the resident K/V
+        buffers are IPC-shared memory freed here, so the stack has no layers left to
+        run afterwards (build a new one)."""
         self._graph = None
+        if self.kv_shared is not None:
+            self.kv_buf, self.k_buf, self.v_buf = [], [], []
         for ex in (self.ex_qkv, self.ex_out, self.kv_shared):
             if ex is not None:
                 ex.close()

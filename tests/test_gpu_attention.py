@@ -72,6 +72,48 @@ def test_tiled_attention_long_lists_and_lse(cuda_ok):
     np.testing.assert_allclose(to_np(lse), ref_lse.reshape(B, H, -1), atol=2e-3, rtol=1e-4)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("pattern", ["even", "odd", "mixed"])
+def test_reference_max_jumps(cuda_ok, dtype, pattern):
+    """Key blocks whose scores jump far above everything before them, at even or
+    odd list positions or both: the reference max moves mid-list (O rescaled,
+    the other softmax group's P recomputed) and the result still matches."""
+    B, H, D, bs, nq, nkb = 1, 2, 128, 128, 3, 12
+    q, _ = rand((B, H, nq * bs, D), 611, dtype)
+    k, _ = rand((B, H, nkb * bs, D), 612, dtype)
+    v, tv = rand((B, H, nkb * bs, D), 613, dtype)
+    pos = {"even": [2, 6, 8], "odd": [3, 5, 9], "mixed": [1, 4, 7, 10]}[pattern]
+    rng = np.random.default_rng(7)
+    idx = np.zeros((B, H, nq, nkb), np.int32)
+    for h in range(H):
+        for i in range(nq):
+            idx[0, h, i] = rng.permutation(nkb)
+    # Block idx[0, h, i, p] at list position p in ``pos`` gets a growing scale: its
+    # scores sit 30-200 log2 units above the earlier blocks of the row.
+    kk = k.reshape(B, H, nkb, bs, D).copy()
+    for h in range(H):
+        for i in range(nq):
+            for n, p in enumerate(pos):
+                kk[0, h, idx[0, h, i, p]] *= 12.0 * (n + 1)
+    # Every row of a head shares one scaled set only when the rows agree; give each
+    # (h, i) its own K copy by making the lists of a head identical.
+    for h in range(H):
+        idx[0, h, 1:] = idx[0, h, 0]
+    kk = kk.reshape(B, H, nkb * bs, D)
+    tk = to_gpu(kk, dtype)
+    tq = to_gpu(q, dtype)
+    cnt = np.full((B, H, nq), nkb, np.int32)
+    out = K.sparse_attn_tiled(tq, tk, tv, torch.from_numpy(idx).to(dev()), torch.from_numpy(cnt).to(dev()), bs)
+    torch.cuda.synchronize()
+    assert K.device_errors() == 0
+    got = to_np(out)
+    kk_r = to_np(tk)
+    ref, _ = O.sparse_attention_tiled(q.reshape(B, H, nq, bs, D), kk_r.reshape(B, H, nkb, bs, D),
+                                      v.reshape(B, H, nkb, bs, D), idx, cnt,
+                                      p_dtype=dtype if dtype == "bf16" else None)
+    assert_close_bf16(got, ref.reshape(B, H, nq * bs, D), what=f"{dtype} {pattern}")
+
+
 def test_tiled_attention_rejects_like_reference(cuda_ok):
     t = torch.zeros((1, 1, 256, 128), device=dev(), dtype=torch.bfloat16)
     k = torch.zeros((1, 1, 200, 128), device=dev(), dtype=torch.bfloat16)
