@@ -282,14 +282,16 @@ __global__ void __launch_bounds__(128) score_kernel(const SelArgs a, uint32_t* _
 }
 
 // Register-tiled scores for the dot metrics (no in-kernel normalisation): a
-// CTA of 256 threads takes 16 query rows x 128 keys; thread (rg, kh, kq) forms
-// rows 4rg..4rg+3 against keys 64kh + kq and 64kh + kq + 32, each with the four
+// CTA of 256 threads takes 16 query rows x 64M keys; thread (rg, kh, kq) forms
+// rows 4rg..4rg+3 against keys 32M kh + kq + 32m (m < M), each with the four
 // interleaved fp64 partial sums of the fixed order. D is staged 32 columns at
 // a time; the next slice's global loads are in flight while the current one
-// is used.
-constexpr int kTileRows = 16, kTileKeys = 128, kTileD = 32, kTileThreads = 256;
-template <int DT>
+// is used. M = 2 (128 keys) normally; M = 1 doubles the CTA count when the
+// grid would otherwise fill fewer than two waves of the GPU (few heads).
+constexpr int kTileRows = 16, kTileKeysMax = 128, kTileD = 32, kTileThreads = 256;
+template <int DT, int M>
 __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs a, uint32_t* __restrict__ keys) {
+  constexpr int kTileKeys = 64 * M;
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int pitch = kTileD + 1;
   double* qs = reinterpret_cast<double*>(smem);          // [kTileRows][pitch]
@@ -329,11 +331,11 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
       for (int e = 0; e < epc; ++e) dst[e] = (double)chunk_elem(pre[l], e, DT);
     }
   };
-  double acc[4][2][4];
+  double acc[4][M][4];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
+    for (int m = 0; m < M; ++m)
 #pragma unroll
       for (int u = 0; u < 4; ++u) acc[r][m][u] = 0.0;
   fetch(0);
@@ -346,15 +348,15 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
     for (int d = 0; d < kTileD; d += 4) {
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        double kv[2], qv[4];
+        double kv[M], qv[4];
 #pragma unroll
-        for (int m = 0; m < 2; ++m) kv[m] = ks[(64 * kh + kq + 32 * m) * pitch + d + u];
+        for (int m = 0; m < M; ++m) kv[m] = ks[(32 * M * kh + kq + 32 * m) * pitch + d + u];
 #pragma unroll
         for (int r = 0; r < 4; ++r) qv[r] = qs[(4 * rg + r) * pitch + d + u];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int m = 0; m < 2; ++m) acc[r][m][u] = fma(qv[r], kv[m], acc[r][m][u]);
+          for (int m = 0; m < M; ++m) acc[r][m][u] = fma(qv[r], kv[m], acc[r][m][u]);
       }
     }
     if (more) {
@@ -369,8 +371,8 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
     if (lr >= nrows) break;
     const int qi = q0 + lr;
 #pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      const int kr = 64 * kh + kq + 32 * m;
+    for (int m = 0; m < M; ++m) {
+      const int kr = 32 * M * kh + kq + 32 * m;
       if (kr >= nkeys) continue;
       const int j = j0 + kr;
       const double dot = ((acc[r][m][0] + acc[r][m][1]) + acc[r][m][2]) + acc[r][m][3];
@@ -381,88 +383,114 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
   }
 }
 
-// One warp per query row: top-k of the precomputed radix keys, emitted sorted.
-// An 8-bit radix select finds the k-th largest key T (key_bits / 8 histogram
-// passes over the row, each followed by a warp scan of 256 bins); one pass in
-// ascending j then emits every key above T and the lowest-index keys equal to
-// T until k are taken — the order of the composite key
+// One CTA of 256 threads per query row: top-k of the precomputed radix keys,
+// emitted sorted. An 8-bit radix select finds the k-th largest key T (key_bits / 8
+// histogram passes over the row in shared memory; thread t owns digit 255 - t
+// and a block scan of the 256 counts finds the digit holding rank k); one pass
+// in ascending j then emits every key above T and the lowest-index keys equal
+// to T until k are taken — the order of the composite key
 // (radix_key << idx_bits) | (2^idx_bits - 1 - j), ties to the lowest index.
-__global__ void __launch_bounds__(128) topk_kernel(const SelArgs a, const uint32_t* __restrict__ keys) {
+// Thread t emits the contiguous keys [t*per, (t+1)*per): block scans of its
+// tie and selection counts give each thread its ties already taken and its
+// output position.
+constexpr int kTopkThreads = 256;
+
+// Exclusive block scan of one value per thread (kTopkThreads threads); *total is
+// the block sum. scratch: 8 words, reusable when the call returns.
+__device__ __forceinline__ uint32_t block_exscan(uint32_t v, uint32_t* scratch, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  if (lane == 31) scratch[warp] = inc;
+  __syncthreads();
+  uint32_t base = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kTopkThreads / 32; ++w) {
+    const uint32_t x = scratch[w];
+    base += w < warp ? x : 0u;
+    tot += x;
+  }
+  __syncthreads();
+  *total = tot;
+  return base + inc - v;
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const SelArgs a, const uint32_t* __restrict__ keys) {
+  static_assert(kTopkThreads == 256, "one thread per radix digit");
   extern __shared__ __align__(16) uint8_t smem[];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int qi = blockIdx.x * 4 + warp, bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  if (qi >= a.Nq) return;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256;
-  uint32_t* rk = reinterpret_cast<uint32_t*>(smem) + 4 * 256 + warp * a.Nk;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem);  // 256 bins
+  uint32_t* scratch = hist + 256;                      // scan scratch, then the found digit
+  uint32_t* rk = hist + 256 + 16;                      // the row's Nk keys
+  const int t = threadIdx.x;
+  const int qi = blockIdx.x, bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
   const uint32_t* src = keys + ((int64_t)bh * a.Nq + qi) * a.Nk;
-  for (int j = lane; j < a.Nk; j += 32) rk[j] = src[j];
-  __syncwarp();
+  for (int j = t; j < a.Nk; j += kTopkThreads) rk[j] = src[j];
+  __syncthreads();
   const int k = a.k_budget;
-  uint32_t T = 0;        // the k-th largest key
-  int ties = 0;          // keys equal to T that are taken
+  uint32_t T = 0;  // the k-th largest key
+  int ties = 0;    // keys equal to T that are taken
   if (k > 0 && k < a.Nk) {
     uint32_t prefix = 0;
-    int need = k;        // rank of the k-th largest within the keys matching `prefix`
+    int need = k;  // rank of the k-th largest within the keys matching `prefix`
     for (int shift = a.key_bits - 8; shift >= 0; shift -= 8) {
       const uint32_t hi = shift + 8 >= 32 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      for (int d = lane; d < 256; d += 32) hist[d] = 0;
-      __syncwarp();
-      for (int j = lane; j < a.Nk; j += 32) {
+      hist[t] = 0;
+      __syncthreads();
+      for (int j = t; j < a.Nk; j += kTopkThreads) {
         const uint32_t key = rk[j];
         if ((key & hi) == prefix) atomicAdd(&hist[(key >> shift) & 0xFFu], 1u);
       }
-      __syncwarp();
-      // Lane l owns digits 255-8l .. 248-8l; counts of larger digits come first.
-      uint32_t c[8], sum = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) { c[e] = hist[255 - 8 * lane - e]; sum += c[e]; }
-      uint32_t before = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, before, o);
-        if (lane >= o) before += t;
+      __syncthreads();
+      // Thread t owns digit 255 - t: counts of larger digits come first.
+      const uint32_t c = hist[255 - t];
+      uint32_t total;
+      const uint32_t before = block_exscan(c, scratch, &total);
+      if ((int)before < need && (int)(before + c) >= need) {
+        scratch[8] = 255u - (uint32_t)t;
+        scratch[9] = (uint32_t)(need - (int)before);
       }
-      before -= sum;     // keys with a larger digit than this lane's range
-      int found = -1, left = 0;
-      if ((int)before < need && (int)(before + sum) >= need) {
-        uint32_t run = before;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (found < 0 && (int)(run + c[e]) >= need) { found = 255 - 8 * lane - e; left = need - (int)run; }
-          run += c[e];
-        }
-      }
-      const unsigned m = __ballot_sync(0xFFFFFFFFu, found >= 0);
-      const int src_lane = m ? __ffs(m) - 1 : 0;
-      const int digit = __shfl_sync(0xFFFFFFFFu, found, src_lane);
-      need = __shfl_sync(0xFFFFFFFFu, left, src_lane);
-      prefix |= (uint32_t)digit << shift;
-      __syncwarp();
+      __syncthreads();
+      prefix |= scratch[8] << shift;
+      need = (int)scratch[9];
+      __syncthreads();
     }
     T = prefix;
     ties = need;
   }
   int32_t* out = a.idx + b * a.i_b + h * a.i_h + (int64_t)qi * a.i_q;
-  for (int t = lane; t < a.ntxt; t += 32) out[(int64_t)t * a.i_s] = t;
-  int pos = 0, eq_seen = 0;
+  for (int x = t; x < a.ntxt; x += kTopkThreads) out[(int64_t)x * a.i_s] = x;
   if (k > 0) {
-    for (int base = 0; base < a.Nk; base += 32) {
-      const int j = base + lane;
-      bool gt = false, eq = false;
-      if (j < a.Nk) {
+    const int per = (a.Nk + kTopkThreads - 1) / kTopkThreads;
+    const int j0 = t * per < a.Nk ? t * per : a.Nk, j1 = j0 + per < a.Nk ? j0 + per : a.Nk;
+    const bool all = k >= a.Nk;
+    uint32_t n_eq = 0;
+    for (int j = j0; j < j1; ++j) n_eq += rk[j] == T ? 1u : 0u;
+    uint32_t total;
+    const uint32_t eq_before = block_exscan(n_eq, scratch, &total);
+    uint32_t n_sel = 0;
+    {
+      uint32_t e = eq_before;
+      for (int j = j0; j < j1; ++j) {
         const uint32_t key = rk[j];
-        gt = key > T;
-        eq = key == T;
+        const bool eq = key == T;
+        n_sel += (all || key > T || (eq && (int)e < ties)) ? 1u : 0u;
+        e += eq ? 1u : 0u;
       }
-      const unsigned em = __ballot_sync(0xFFFFFFFFu, eq);
-      const bool sel = j < a.Nk && ((k >= a.Nk) || gt || (eq && eq_seen + __popc(em & ((1u << lane) - 1u)) < ties));
-      const unsigned m = __ballot_sync(0xFFFFFFFFu, sel);
-      if (sel) out[(int64_t)(a.ntxt + pos + __popc(m & ((1u << lane) - 1u))) * a.i_s] = j + a.ntxt;
-      pos += __popc(m);
-      eq_seen += __popc(em);
+    }
+    uint32_t pos = block_exscan(n_sel, scratch, &total);
+    uint32_t e = eq_before;
+    for (int j = j0; j < j1; ++j) {
+      const uint32_t key = rk[j];
+      const bool eq = key == T;
+      if (all || key > T || (eq && (int)e < ties)) out[(int64_t)(a.ntxt + (int)pos++) * a.i_s] = j + a.ntxt;
+      e += eq ? 1u : 0u;
     }
   }
-  if (lane == 0) a.cnt[b * a.c_b + h * a.c_h + (int64_t)qi * a.c_q] = a.ntxt + k;
+  if (t == 0) a.cnt[b * a.c_b + h * a.c_h + (int64_t)qi * a.c_q] = a.ntxt + k;
 }
 
 li_status budget_of(const li_select_params* p, int64_t nq, int64_t nk, int32_t* ntxt, int32_t* kb,
@@ -709,6 +737,13 @@ li_status prepare_select(const li_view4* q_pool, const li_view4* k_pool, const l
   return LI_OK;
 }
 
+// SMs of the current device (148 on B200 when the query fails).
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
 // Key scratch of the two-kernel path: B*H*Nq*Nk 32-bit keys. Saturates at
 // INT64_MAX instead of overflowing (no caller can hold that much).
 int64_t select_ws_bytes(int64_t B, int64_t H, int64_t Nq, int64_t Nk) {
@@ -719,8 +754,8 @@ int64_t select_ws_bytes(int64_t B, int64_t H, int64_t Nq, int64_t Nk) {
   return n;
 }
 
-// Shared memory of topk_kernel: four warps' 256-bin histograms and key rows.
-size_t topk_smem(int64_t Nk) { return (size_t)4 * 256 * 4 + (size_t)16 * Nk; }
+// Shared memory of topk_kernel: the 256-bin histogram, scan scratch and the key row.
+size_t topk_smem(int64_t Nk) { return (size_t)(256 + 16) * 4 + (size_t)4 * Nk; }
 
 // Single-kernel selection (no workspace).
 li_status launch_single(SelArgs& a, int64_t B, int64_t H, cudaStream_t s) {
@@ -760,15 +795,25 @@ li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStrea
                    128, smem1, s>>>(a, keys);
     if (li_status st = launched("score_kernel launch")) return st;
   } else {
-    const size_t smem1 = (size_t)(kTileRows + kTileKeys) * (kTileD + 1) * 8;
-    const dim3 grid((unsigned)ceil_div(a.Nq, kTileRows), (unsigned)ceil_div(a.Nk, kTileKeys), (unsigned)(B * H));
-    if (a.dtype == LI_DTYPE_BF16) score_tile_kernel<LI_DTYPE_BF16><<<grid, kTileThreads, smem1, s>>>(a, keys);
-    else if (a.dtype == LI_DTYPE_FP16) score_tile_kernel<LI_DTYPE_FP16><<<grid, kTileThreads, smem1, s>>>(a, keys);
-    else score_tile_kernel<LI_DTYPE_FP32><<<grid, kTileThreads, smem1, s>>>(a, keys);
+    // 128-key tiles unless they leave the grid under two waves of the GPU.
+    const int64_t ctas128 = ceil_div(a.Nq, kTileRows) * ceil_div(a.Nk, kTileKeysMax) * B * H;
+    const int M = ctas128 < 2 * (int64_t)sm_count() ? 1 : 2;
+    const int tile_keys = 64 * M;
+    const size_t smem1 = (size_t)(kTileRows + tile_keys) * (kTileD + 1) * 8;
+    const dim3 grid((unsigned)ceil_div(a.Nq, kTileRows), (unsigned)ceil_div(a.Nk, tile_keys), (unsigned)(B * H));
+    if (M == 1) {
+      if (a.dtype == LI_DTYPE_BF16) score_tile_kernel<LI_DTYPE_BF16, 1><<<grid, kTileThreads, smem1, s>>>(a, keys);
+      else if (a.dtype == LI_DTYPE_FP16) score_tile_kernel<LI_DTYPE_FP16, 1><<<grid, kTileThreads, smem1, s>>>(a, keys);
+      else score_tile_kernel<LI_DTYPE_FP32, 1><<<grid, kTileThreads, smem1, s>>>(a, keys);
+    } else {
+      if (a.dtype == LI_DTYPE_BF16) score_tile_kernel<LI_DTYPE_BF16, 2><<<grid, kTileThreads, smem1, s>>>(a, keys);
+      else if (a.dtype == LI_DTYPE_FP16) score_tile_kernel<LI_DTYPE_FP16, 2><<<grid, kTileThreads, smem1, s>>>(a, keys);
+      else score_tile_kernel<LI_DTYPE_FP32, 2><<<grid, kTileThreads, smem1, s>>>(a, keys);
+    }
     if (li_status st = launched("score_tile_kernel launch")) return st;
   }
   const size_t smem2 = topk_smem(a.Nk);
-  topk_kernel<<<dim3((unsigned)ceil_div(a.Nq, 4), (unsigned)(B * H)), 128, smem2, s>>>(a, keys);
+  topk_kernel<<<dim3((unsigned)a.Nq, (unsigned)(B * H)), kTopkThreads, smem2, s>>>(a, keys);
   return launched("topk_kernel launch");
 }
 }  // namespace

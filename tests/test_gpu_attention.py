@@ -76,8 +76,9 @@ def test_tiled_attention_long_lists_and_lse(cuda_ok):
 @pytest.mark.parametrize("pattern", ["even", "odd", "mixed"])
 def test_reference_max_jumps(cuda_ok, dtype, pattern):
     """Key blocks whose scores jump far above everything before them, at even or
-    odd list positions or both: the reference max moves mid-list (O rescaled,
-    the other softmax group's P recomputed) and the result still matches."""
+    odd list positions (one softmax chain or the other) or both: a chain's
+    reference max moves mid-list, its O is rescaled, and the result still
+    matches."""
     B, H, D, bs, nq, nkb = 1, 2, 128, 128, 3, 12
     q, _ = rand((B, H, nq * bs, D), 611, dtype)
     k, _ = rand((B, H, nkb * bs, D), 612, dtype)
