@@ -354,14 +354,26 @@ def run_gpu(args, cfg, rank, world, local_rank):
     attn_timing["on"] = False
     n_launch = per_step_launches * args.steps if args.graph else L.kernel_launches() - launches0
     ms = start.elapsed_time(end)
-    if args.graph:
-        # The attention kernel's events come from one eager step (same kernels,
-        # same inputs) after the timed region.
-        attn_timing["on"] = True
-        stack.step(x0)
-        attn_timing["on"] = False
-        barrier()
+    # One eager step after the timed region (same kernels, same inputs) gives the
+    # per-layer phase breakdown of this rank and, with --graph, the attention
+    # kernel's events.
+    marks = []
+    attn_timing["on"] = args.graph
+    stack.step(x0, marks=marks)
+    attn_timing["on"] = False
+    barrier()
     attn_ms = [a.elapsed_time(b) for a, b in attn_timing["events"]]
+    breakdown = {}
+    prev = None
+    for name, ev in marks:
+        if name != "start":
+            breakdown[name] = breakdown.get(name, 0.0) + prev.elapsed_time(ev) / cfg.layers
+        prev = ev
+    if attn_ms:
+        a_ms = sum(attn_ms) / len(attn_ms)
+        breakdown["selection"] = breakdown.pop("selection_and_attention") - a_ms
+        breakdown["attention_kernel_and_combine"] = a_ms
+    breakdown = {k: round(v, 4) for k, v in breakdown.items()}
     # End-to-end: host input -> device, step, device output -> host, all on the
     # step's stream; the copies also get their own events.
     x_host = x0.cpu().pin_memory()
@@ -434,6 +446,9 @@ def run_gpu(args, cfg, rank, world, local_rank):
                 "h2d_ms_per_step": h2d_ms, "d2h_ms_per_step": d2h_ms},
         "gpu_launches": int(n_launch * world),
         "clocks": clk.summary(),
+        # Rank 0's mean ms per layer by phase, from one eager step (exchanges include
+        # waiting for the other ranks).
+        "layer_breakdown_ms": breakdown,
     }
     if exch is not None:
         line["exchange_check"] = exch["check"]

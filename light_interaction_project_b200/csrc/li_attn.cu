@@ -777,6 +777,7 @@ struct CombineArgs {
 };
 
 __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const CombineArgs a) {
+  static_assert(kCombRows * kMaxPieces == kCombThreads, "one thread per (row, piece) in the weight pass");
   __shared__ float wgt[kMaxPieces][kCombRows];
   __shared__ int64_t tok_s[kCombRows];
   const int64_t tile = a.n_whole + blockIdx.x;
@@ -788,50 +789,55 @@ __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const Combin
   const int64_t unit0 = (int64_t)blockIdx.x * a.nsplit;
   const float* pm = a.part + a.part_units * 128 * a.D;
   const float* pl = pm + a.part_units * 128;
-  if (threadIdx.x < kCombRows) {
-    const int row = r0 + threadIdx.x;
-    // Row of the full query block (sub-blocks halve dimension q_split).
-    int frow = row;
-    if (a.sub > 1) {
-      if (!a.q_raster) {
-        frow = qs * a.bsk + row;
-      } else {
-        int tw = a.tw, th = a.th, tt = a.tt;
-        if (a.q_split == 1) tw /= 2;
-        else if (a.q_split == 2) th /= 2;
-        else tt /= 2;
-        int ow = row % tw, rr = row / tw, oh = rr % th, ot = rr / th;
-        if (a.q_split == 1) ow += qs * tw;
-        else if (a.q_split == 2) oh += qs * th;
-        else ot += qs * tt;
-        frow = (ot * a.th + oh) * a.tw + ow;
-      }
-    }
-    int64_t tok;
-    if (a.q_raster) {
-      const int cw = qi % a.nw, rem = qi / a.nw, ch = rem % a.nh, ct = rem / a.nh;
-      const int ow = frow % a.tw, rr = frow / a.tw, oh = rr % a.th, ot = rr / a.th;
-      const int t = ct * a.tt + ot, hh = ch * a.th + oh, w = cw * a.tw + ow;
-      tok = (t < a.T && hh < a.LH && w < a.LW) ? ((int64_t)t * a.LH + hh) * a.LW + w : -1;
-    } else {
-      tok = (int64_t)qi * a.bs + frow;
-      if (tok >= a.q_len) tok = -1;
-    }
-    tok_s[threadIdx.x] = tok;
-    float M = -INFINITY;
-    for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, pm[(unit0 + sp) * 128 + row]);
-    float L = 0.f;
-    for (int sp = 0; sp < a.nsplit; ++sp) {
-      const float l = pl[(unit0 + sp) * 128 + row];
-      if (l > 0.f) L += ex2(pm[(unit0 + sp) * 128 + row] - M) * l;
-    }
+  {
+    // Weight pass: thread (lr, sp) holds piece sp of row r0 + lr; the 16 pieces
+    // of a row are 16 adjacent lanes, reduced with shuffles.
+    const int lr = threadIdx.x / kMaxPieces, sp = threadIdx.x % kMaxPieces;
+    const int row = r0 + lr;
+    const bool have = sp < a.nsplit;
+    const float m = have ? pm[(unit0 + sp) * 128 + row] : -INFINITY;
+    const float l = have ? pl[(unit0 + sp) * 128 + row] : 0.f;
+    float M = l > 0.f ? m : -INFINITY;
+#pragma unroll
+    for (int o = kMaxPieces / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    const float e = l > 0.f ? ex2(m - M) : 0.f;
+    float L = e * l;
+#pragma unroll
+    for (int o = kMaxPieces / 2; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    for (int sp = 0; sp < a.nsplit; ++sp) {
-      const float l = pl[(unit0 + sp) * 128 + row];
-      wgt[sp][threadIdx.x] = l > 0.f ? ex2(pm[(unit0 + sp) * 128 + row] - M) * inv : 0.f;
+    wgt[sp][lr] = e * inv;
+    if (sp == 0) {
+      // Row of the full query block (sub-blocks halve dimension q_split).
+      int frow = row;
+      if (a.sub > 1) {
+        if (!a.q_raster) {
+          frow = qs * a.bsk + row;
+        } else {
+          int tw = a.tw, th = a.th, tt = a.tt;
+          if (a.q_split == 1) tw /= 2;
+          else if (a.q_split == 2) th /= 2;
+          else tt /= 2;
+          int ow = row % tw, rr = row / tw, oh = rr % th, ot = rr / th;
+          if (a.q_split == 1) ow += qs * tw;
+          else if (a.q_split == 2) oh += qs * th;
+          else ot += qs * tt;
+          frow = (ot * a.th + oh) * a.tw + ow;
+        }
+      }
+      int64_t tok;
+      if (a.q_raster) {
+        const int cw = qi % a.nw, rem = qi / a.nw, ch = rem % a.nh, ct = rem / a.nh;
+        const int ow = frow % a.tw, rr = frow / a.tw, oh = rr % a.th, ot = rr / a.th;
+        const int t = ct * a.tt + ot, hh = ch * a.th + oh, w = cw * a.tw + ow;
+        tok = (t < a.T && hh < a.LH && w < a.LW) ? ((int64_t)t * a.LH + hh) * a.LW + w : -1;
+      } else {
+        tok = (int64_t)qi * a.bs + frow;
+        if (tok >= a.q_len) tok = -1;
+      }
+      tok_s[lr] = tok;
+      if (a.lse && tok >= 0)
+        a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + frow] = L > 0.f ? M + __log2f(L) : -INFINITY;
     }
-    if (a.lse && tok >= 0)
-      a.lse[(int64_t)bh * a.lse_len + (int64_t)qi * a.bs + frow] = L > 0.f ? M + __log2f(L) : -INFINITY;
   }
   __syncthreads();
   const int cpr = a.D / 8;  // 8-column chunks per row
@@ -841,13 +847,27 @@ __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const Combin
     if (tok < 0) continue;
     const int row = r0 + lr;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int sp = 0; sp < a.nsplit; ++sp) {
-      const float w = wgt[sp][lr];
-      if (w == 0.f) continue;
-      const float4* src = reinterpret_cast<const float4*>(a.part + ((unit0 + sp) * 128 + row) * a.D + d0);
-      const float4 x = src[0], y = src[1];
-      acc[0] += w * x.x; acc[1] += w * x.y; acc[2] += w * x.z; acc[3] += w * x.w;
-      acc[4] += w * y.x; acc[5] += w * y.y; acc[6] += w * y.z; acc[7] += w * y.w;
+    // Pieces in groups of 8: a group's 16 loads are all issued before they are
+    // used (indices past nsplit re-read the last piece with weight 0; a zero
+    // weight selects 0, so an unwritten partial cannot leak into the row).
+    for (int g0 = 0; g0 < a.nsplit; g0 += 8) {
+      float4 x[8], y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int sp = min(g0 + e, a.nsplit - 1);
+        const float4* src = reinterpret_cast<const float4*>(a.part + ((unit0 + sp) * 128 + row) * a.D + d0);
+        x[e] = src[0];
+        y[e] = src[1];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float w = g0 + e < a.nsplit ? wgt[g0 + e][lr] : 0.f;
+        const bool on = w != 0.f;
+        acc[0] += on ? w * x[e].x : 0.f; acc[1] += on ? w * x[e].y : 0.f;
+        acc[2] += on ? w * x[e].z : 0.f; acc[3] += on ? w * x[e].w : 0.f;
+        acc[4] += on ? w * y[e].x : 0.f; acc[5] += on ? w * y[e].y : 0.f;
+        acc[6] += on ? w * y[e].z : 0.f; acc[7] += on ? w * y[e].w : 0.f;
+      }
     }
     uint4 v;
     if (a.f16) {

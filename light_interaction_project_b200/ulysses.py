@@ -424,11 +424,22 @@ class HeadShardedStack:
             K.gather_frames(full[:, 2].permute(1, 2, 0, 3), self.chunk_frames, ft, out=self.v_buf[i][:, :, tail:])
         return full[:, 0].permute(1, 2, 0, 3)                                    # [B, hl, S, D] view
 
-    def layer(self, i: int, x: torch.Tensor, attn_events=None) -> torch.Tensor:
+    def layer(self, i: int, x: torch.Tensor, attn_events=None, marks=None) -> torch.Tensor:
+        """Layer ``i``. ``marks`` (optional list): a timing event is recorded on the
+        current stream before the layer and after each of its phases and appended as
+        ``(phase, event)``: qkv_projection_and_exchange, pooling,
+        selection_and_attention, output_exchange, o_projection."""
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
         cfg = self.cfg
         B, s, _ = x.shape
         S = s * self.world
+        mark("start")
         q = self.qkv_exchange(i, x)
+        mark("qkv_projection_and_exchange")
         # The attention writes its output token-major ([B, S, H/P, D]), the order the
         # return all-to-all / O projection reads, so no re-layout copy follows.
         o_tok = torch.empty(B, S, self.hl, cfg.head_dim, device=x.device, dtype=x.dtype)
@@ -443,6 +454,7 @@ class HeadShardedStack:
         if kjob is not None:
             jobs.append(kjob)
         K.pool_blocks_multi(jobs)
+        mark("pooling")
         if attn_events is not None:
             attn_events[0].record()
         o = mg.run_sparse_attention(q, self.k_buf[i], self.v_buf[i], 0, i, cfg.latent_hw, self.params,
@@ -450,15 +462,19 @@ class HeadShardedStack:
                                     k_pool=self.key_pools[i], q_pool=q_pool)
         if attn_events is not None:
             attn_events[1].record()
+        mark("selection_and_attention")
         if self.ex_out is not None:
             row = self.hl * cfg.head_dim * o_tok.element_size()
             recv = self.ex_out.push(o_tok, s, row, s * row, row, self.rank * row, cfg.heads * row // self.hl)
             back = recv[: s * cfg.heads * cfg.head_dim].view(B, s, cfg.heads, cfg.head_dim)
         else:
             back = head_to_seq(o, self.world, self.group)                       # [B, s, H, D]
+        mark("output_exchange")
         # O projection with the residual add in the GEMM epilogue.
-        return torch.addmm(x.reshape(B * s, cfg.hidden), back.reshape(B * s, cfg.heads * cfg.head_dim),
-                           self.w_o[i]).view(B, s, cfg.hidden)
+        y = torch.addmm(x.reshape(B * s, cfg.hidden), back.reshape(B * s, cfg.heads * cfg.head_dim),
+                        self.w_o[i]).view(B, s, cfg.hidden)
+        mark("o_projection")
+        return y
 
     def close(self):
         """Releases the captured graph and the peer-exchange buffers (after the last
@@ -473,13 +489,14 @@ class HeadShardedStack:
                 ex.close()
         self.ex_qkv = self.ex_out = self.kv_shared = None
 
-    def step(self, x: torch.Tensor, attn_events=None, check_errors: bool = False) -> torch.Tensor:
+    def step(self, x: torch.Tensor, attn_events=None, check_errors: bool = False, marks=None) -> torch.Tensor:
         """One step of every layer. ``check_errors``: synchronise afterwards and raise if
         a kernel reported a device-side error (a bad block id, a bounded wait that
         gave up); device errors are otherwise only visible through
-        ``kernels.raise_device_errors``."""
+        ``kernels.raise_device_errors``. ``marks``: per-phase timing events of every
+        layer (see :meth:`layer`)."""
         for i in range(self.cfg.layers):
-            x = self.layer(i, x, attn_events[i] if attn_events is not None else None)
+            x = self.layer(i, x, attn_events[i] if attn_events is not None else None, marks)
         if check_errors:
             K.raise_device_errors(self.device)
         return x
