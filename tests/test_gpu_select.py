@@ -27,6 +27,10 @@ DECODE_CASES = [
     ("fp32", "scaled_dot_product", (1, 2, 1), (3, 2, 1), (2, 4, 8), 0, 2, 0.5, None),
     ("bf16", "cosine", (1, 1, 2), (1, 1, 2), (1, 8, 16), 0, 9, 0.3, None),   # protect > available
     ("bf16", "scaled_dot_product", (1, 4, 4), (64, 4, 4), (1, 8, 16), 0, 1, 0.1, 2),  # 1024 key blocks
+    # 3040 key blocks (12 per top-k thread, not a multiple of 256), quantised: ties span thread slices
+    ("bf16", "scaled_dot_product", (1, 4, 4), (190, 4, 4), (1, 8, 16), 0, 1, 0.1, 2),
+    # 2800 key blocks with 32-bit radix keys (four 8-bit passes)
+    ("fp32", "dot", (1, 2, 2), (700, 2, 2), (2, 4, 8), 0, 2, 0.3, 4),
 ]
 
 
