@@ -14,8 +14,9 @@ pools, copy padded text K/V, tile+pool Q and K/V (Triton), select blocks
    q's raster layout (plus a combine kernel when the last wave's tiles are
    split).
 
-Five to seven kernel launches, no host synchronisation, no intermediate tiled
-tensors.
+Four to six kernel launches (the key pooling is skipped when a key-pool cache
+holds it; the combine runs only for a split tail), no host synchronisation, no
+intermediate tiled tensors.
 """
 
 from __future__ import annotations
