@@ -290,12 +290,14 @@ __global__ void __launch_bounds__(128) score_kernel(const SelArgs a, uint32_t* _
 // grid would otherwise fill fewer than two waves of the GPU (few heads).
 constexpr int kTileRows = 16, kTileKeysMax = 128, kTileD = 32, kTileThreads = 256;
 template <int DT, int M>
-__global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs a, uint32_t* __restrict__ keys) {
+__global__ void __launch_bounds__(kTileThreads, 2) score_tile_kernel(const SelArgs a, uint32_t* __restrict__ keys) {
   constexpr int kTileKeys = 64 * M;
   extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int pitch = kTileD + 1;
-  double* qs = reinterpret_cast<double*>(smem);          // [kTileRows][pitch]
-  double* ks = qs + kTileRows * pitch;                   // [kTileKeys][pitch]
+  // K rows: odd pitch, so a warp's 32 keys hit distinct bank pairs. Q rows: even
+  // pitch, so a thread reads two consecutive d of a row as one 16-byte broadcast.
+  constexpr int pitch = kTileD + 1, qpitch = kTileD + 2;
+  double* qs = reinterpret_cast<double*>(smem);          // [kTileRows][qpitch]
+  double* ks = qs + kTileRows * qpitch;                  // [kTileKeys][pitch]
   const int bh = blockIdx.z, b = bh / a.H, h = bh % a.H;
   const int q0 = blockIdx.x * kTileRows, j0 = blockIdx.y * kTileKeys;
   const int nrows = min(kTileRows, a.Nq - q0), nkeys = min(kTileKeys, a.Nk - j0);
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
       const int i = tid + l * kTileThreads;
       const int r = i / CHD, c = i % CHD;
       if (r >= kTileRows + kTileKeys) continue;
-      double* dst = (r < kTileRows ? qs + r * pitch : ks + (r - kTileRows) * pitch) + c * epc;
+      double* dst = (r < kTileRows ? qs + r * qpitch : ks + (r - kTileRows) * pitch) + c * epc;
 #pragma unroll
       for (int e = 0; e < epc; ++e) dst[e] = (double)chunk_elem(pre[l], e, DT);
     }
@@ -347,16 +349,21 @@ __global__ void __launch_bounds__(kTileThreads) score_tile_kernel(const SelArgs 
 #pragma unroll 2
     for (int d = 0; d < kTileD; d += 4) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        double kv[M], qv[4];
+      for (int u2 = 0; u2 < 4; u2 += 2) {
+        double2 q2[4];
 #pragma unroll
-        for (int m = 0; m < M; ++m) kv[m] = ks[(32 * M * kh + kq + 32 * m) * pitch + d + u];
+        for (int r = 0; r < 4; ++r) q2[r] = *reinterpret_cast<const double2*>(qs + (4 * rg + r) * qpitch + d + u2);
 #pragma unroll
-        for (int r = 0; r < 4; ++r) qv[r] = qs[(4 * rg + r) * pitch + d + u];
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int u = u2 + h2;
+          double kv[M];
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+          for (int m = 0; m < M; ++m) kv[m] = ks[(32 * M * kh + kq + 32 * m) * pitch + d + u];
 #pragma unroll
-          for (int m = 0; m < M; ++m) acc[r][m][u] = fma(qv[r], kv[m], acc[r][m][u]);
+          for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[r][m][u] = fma(h2 ? q2[r].y : q2[r].x, kv[m], acc[r][m][u]);
+        }
       }
     }
     if (more) {
@@ -799,7 +806,7 @@ li_status launch_two(SelArgs& a, int64_t B, int64_t H, uint32_t* keys, cudaStrea
     const int64_t ctas128 = ceil_div(a.Nq, kTileRows) * ceil_div(a.Nk, kTileKeysMax) * B * H;
     const int M = ctas128 < 2 * (int64_t)sm_count() ? 1 : 2;
     const int tile_keys = 64 * M;
-    const size_t smem1 = (size_t)(kTileRows + tile_keys) * (kTileD + 1) * 8;
+    const size_t smem1 = ((size_t)kTileRows * (kTileD + 2) + (size_t)tile_keys * (kTileD + 1)) * 8;
     const dim3 grid((unsigned)ceil_div(a.Nq, kTileRows), (unsigned)ceil_div(a.Nk, tile_keys), (unsigned)(B * H));
     if (M == 1) {
       if (a.dtype == LI_DTYPE_BF16) score_tile_kernel<LI_DTYPE_BF16, 1><<<grid, kTileThreads, smem1, s>>>(a, keys);
