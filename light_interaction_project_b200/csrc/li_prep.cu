@@ -67,7 +67,7 @@ __device__ __forceinline__ int64_t token_of(const TileArgs& a, int blk, int r, b
   return (f * a.LH + h) * (int64_t)a.LW + w;
 }
 
-constexpr int kMaxBS = 1024;
+constexpr int kMaxBS = 1024;  // tokens per 3D block (the pooling CTA's row table)
 
 // DT is the element type (LI_DTYPE_*), fixed at compile time so the per-element
 // widening carries no dtype branches.
@@ -273,7 +273,8 @@ li_status check_grid(const li_grid3d& g) {
     return fail(LI_ERR_SHAPE, "grid dims must be positive (T=%d LH=%d LW=%d tile=%d,%d,%d)", g.T, g.LH,
                 g.LW, g.tt, g.th, g.tw);
   const int bs = g.tt * g.th * g.tw;
-  if (bs % 8 || bs > 1024) return fail(LI_ERR_UNSUPPORTED, "block size %d must be a multiple of 8 and <= 1024", bs);
+  if (bs % 8 || bs > kMaxBS)
+    return fail(LI_ERR_UNSUPPORTED, "block size %d must be a multiple of 8 and <= %d", bs, kMaxBS);
   return LI_OK;
 }
 
@@ -448,7 +449,7 @@ extern "C" li_status li_text_blocks(const li_view4* src0, const li_view4* src1, 
                                     li_view5* dst0, li_view5* dst1, void* stream) {
   if (!src0 || !dst0) return fail(LI_ERR_INVALID_ARG, "src0 and dst0 are required");
   if ((src1 == nullptr) != (dst1 == nullptr)) return fail(LI_ERR_INVALID_ARG, "dst1 must be given iff src1 is");
-  if (bs <= 0 || bs % 8 || bs > 1024) return fail(LI_ERR_UNSUPPORTED, "block size %d", bs);
+  if (bs <= 0 || bs % 8 || bs > kMaxBS) return fail(LI_ERR_UNSUPPORTED, "block size %d", bs);
   const int64_t B = src0->shape[0], H = src0->shape[1], N = src0->shape[2], D = src0->shape[3];
   if (N == 0) return LI_OK;
   const int dtype = src0->dtype;
